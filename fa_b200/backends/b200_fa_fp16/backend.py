@@ -1,0 +1,44 @@
+"""b200_fa_fp16 -- sm_100a flash-attention forward, FP16 softmax variant.
+
+The B200 counterpart of the reference's CCE FP16 backend
+(backends/cce_fa_nqkq_nz_resident_v13_q768_pool_i4_p128): FP16 exponent
+arguments, FP16 exp2 (two per MUFU operation) and FP16 partial row sums;
+P in FP16 for the PV product; O accumulated in FP32 in tensor memory and
+normalized in FP32 before the FP16 store.
+
+External-type backend (core/drivers/external.py contract): ``build`` runs the
+hash-keyed nvcc build (CPU-safe, idempotent), ``adapt`` binds the canonical
+tensors, ``call`` launches the kernel through libb200fa.so and returns O
+[B,Hq,Nq,128] FP16 on the inputs' device.  The kernel symbol
+``b200_fa_fp16_kernel`` contains this directory's name, which is how the
+harness profiler attributes device time to this backend.
+"""
+
+from fa_b200.core.contract import Meta
+
+VARIANT = "fp16"
+
+META = Meta(
+    name="b200_fa_fp16",
+    type="external",
+    op_type="b200_fa_fp16_kernel",
+    author="fa_b200",
+    notes="tcgen05/TMEM warp-specialised FA forward; FP16 exp/partial sums, FP32 O in TMEM",
+)
+
+
+def build(case):
+    from fa_b200 import build as nvcc_build
+
+    nvcc_build.build()
+
+
+def adapt(case, canonical):
+    from fa_b200.ops import Operator
+
+    return {"q": canonical["q"], "k": canonical["k"], "v": canonical["v"],
+            "scale": case.scale, "op": Operator(VARIANT)}
+
+
+def call(op_args):
+    return op_args["op"](op_args["q"], op_args["k"], op_args["v"], scale=op_args["scale"])

@@ -1,0 +1,262 @@
+// b200fa.cu -- host side of libb200fa.so: argument validation, TMA tensor
+// maps, persistent-grid launch and the C ABI declared in include/b200fa.h.
+//
+// Replaces the reference CCE backends' native layers:
+//   * shape/dtype checks of binding.py:87-98 and op_host/*.cpp:8-19
+//     -> validate() below, returning negative codes instead of raising;
+//   * ACLNN GetWorkspaceSize/launch pair (binding.py:20-26, 72-80) and the
+//     host tiling Tile() (op_host/*.cpp:53-89) -> b200fa_fwd / _fwd_ex;
+//   * PartitionContiguous (cce_task.h:28-35) -> b200fa_partition.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "b200fa.h"
+#include "fa_kernel.cuh"
+
+using namespace b200fa;
+
+__global__ void __launch_bounds__(kThreads, 1) b200_fa_fp16_kernel(const __grid_constant__ FwdParams p) {
+  attention_fwd_body<0>(p);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) b200_fa_fp32_kernel(const __grid_constant__ FwdParams p) {
+  attention_fwd_body<1>(p);
+}
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(static_cast<int>(e), "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+constexpr int64_t kMax31 = (int64_t(1) << 31) - 1;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Per-device facts read once: SM count, kernel attributes set.
+struct DeviceState {
+  std::once_flag once;
+  int sms = 0;
+  cudaError_t err = cudaSuccess;
+};
+DeviceState g_devices[64];
+
+int device_setup(int dev, int* sms) {
+  if (dev < 0 || dev >= 64) return fail(B200FA_ERR_OPTIONS, "device ordinal %d out of range", dev);
+  DeviceState& d = g_devices[dev];
+  std::call_once(d.once, [&d, dev] {
+    cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(b200_fa_fp16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(b200_fa_fp32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    d.err = e;
+  });
+  if (d.err != cudaSuccess) return cuda_fail(d.err, "device setup");
+  *sms = d.sms;
+  return B200FA_OK;
+}
+
+int validate_shape(int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, int64_t Nk, int64_t D) {
+  if (D != kHeadDim) return fail(B200FA_ERR_HEAD_DIM, "head dim must be 128, got %lld", (long long)D);
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Nq <= 0 || Nk <= 0)
+    return fail(B200FA_ERR_SHAPE, "invalid attention geometry B=%lld Hq=%lld Hkv=%lld Nq=%lld Nk=%lld",
+                (long long)B, (long long)Hq, (long long)Hkv, (long long)Nq, (long long)Nk);
+  if (Hq % Hkv != 0)
+    return fail(B200FA_ERR_GROUPING, "Hq (%lld) must be a multiple of Hkv (%lld)", (long long)Hq, (long long)Hkv);
+  if (Nq > kMax31 || Nk > kMax31 || B * Hq > kMax31 || B * Hkv > kMax31)
+    return fail(B200FA_ERR_TOO_LARGE, "Nq, Nk and B*H must be below 2^31");
+  const int64_t units = B * Hq * ceil_div<int64_t>(Nq, kBlockM);
+  if (units > kMax31) return fail(B200FA_ERR_TOO_LARGE, "work unit count %lld exceeds 2^31-1", (long long)units);
+  return B200FA_OK;
+}
+
+int encode_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t planes) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return fail(B200FA_ERR_NO_DRIVER, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[3] = {cuuint64_t(kHeadDim), cuuint64_t(rows), cuuint64_t(planes)};
+  const cuuint64_t strides[2] = {cuuint64_t(kHeadDim * 2), cuuint64_t(rows) * kHeadDim * 2};
+  const cuuint32_t box[3] = {64, cuuint32_t(kBlockM), 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200FA_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return B200FA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int64_t b200fa_num_units(int64_t B, int64_t Hq, int64_t Nq) {
+  if (B <= 0 || Hq <= 0 || Nq <= 0) return fail(B200FA_ERR_SHAPE, "non-positive size");
+  return B * Hq * ceil_div<int64_t>(Nq, kBlockM);
+}
+
+int b200fa_partition(int64_t total, int32_t parts, int32_t index, int64_t* begin, int64_t* end) {
+  if (!begin || !end) return fail(B200FA_ERR_NULL, "begin/end must not be NULL");
+  if (total < 0 || parts <= 0 || index < 0 || index >= parts)
+    return fail(B200FA_ERR_UNIT_RANGE, "bad partition total=%lld parts=%d index=%d", (long long)total, parts, index);
+  const int64_t base = total / parts, rem = total % parts;
+  *begin = index * base + (index < rem ? index : rem);
+  *end = *begin + base + (index < rem ? 1 : 0);
+  return B200FA_OK;
+}
+
+int64_t b200fa_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, int64_t Nk, int64_t D,
+                              int32_t variant) {
+  const int rc = validate_shape(B, Hq, Hkv, Nq, Nk, D);
+  if (rc != B200FA_OK) return rc;
+  if (variant != B200FA_VARIANT_FP16 && variant != B200FA_VARIANT_FP32)
+    return fail(B200FA_ERR_VARIANT, "unknown variant %d", variant);
+  return int64_t(B200FA_WS_HEADER_BYTES) + int64_t(B200FA_WS_TRACE_BYTES) * B200FA_MAX_CTAS;
+}
+
+int64_t b200fa_plan_item(int64_t B, int64_t Hq, int64_t Nq, int64_t unit_begin, int64_t unit_end, int64_t index,
+                         int64_t* bh, int64_t* qblock, int64_t* count) {
+  const int64_t units = b200fa_num_units(B, Hq, Nq);
+  if (units < 0) return units;
+  if (unit_begin < 0 || unit_end > units || unit_begin > unit_end)
+    return fail(B200FA_ERR_UNIT_RANGE, "unit range [%lld, %lld) outside [0, %lld)", (long long)unit_begin,
+                (long long)unit_end, (long long)units);
+  const int64_t nqb = ceil_div<int64_t>(Nq, kBlockM);
+  const int64_t n = plan_count<int64_t>(nqb, unit_begin, unit_end);
+  if (index >= 0 && index < n && bh && qblock && count) plan_decode<int64_t>(nqb, unit_begin, unit_end, index, *bh, *qblock, *count);
+  return n;
+}
+
+int b200fa_fwd_ex(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq, int64_t Hkv,
+                  int64_t Nq, int64_t Nk, int64_t D, float scale, int32_t variant, int64_t unit_begin,
+                  int64_t unit_end, void* workspace, uint64_t ws_bytes, void* stream, const b200fa_options* opts) {
+  g_last_error[0] = '\0';
+  if (!q || !k || !v || !o) return fail(B200FA_ERR_NULL, "q, k, v and o must be device pointers");
+  int rc = validate_shape(B, Hq, Hkv, Nq, Nk, D);
+  if (rc != B200FA_OK) return rc;
+  if (variant != B200FA_VARIANT_FP16 && variant != B200FA_VARIANT_FP32)
+    return fail(B200FA_ERR_VARIANT, "unknown variant %d", variant);
+  if (!std::isfinite(scale) || !(scale > 0.f)) return fail(B200FA_ERR_SCALE, "scale must be finite and positive");
+  const int64_t units = B * Hq * ceil_div<int64_t>(Nq, kBlockM);
+  if (unit_begin < 0 || unit_end > units || unit_begin > unit_end)
+    return fail(B200FA_ERR_UNIT_RANGE, "unit range [%lld, %lld) outside [0, %lld)", (long long)unit_begin,
+                (long long)unit_end, (long long)units);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(B200FA_ERR_ALIGNMENT, "tensor pointers must be 16-byte aligned");
+  const uint64_t ws_need = uint64_t(B200FA_WS_HEADER_BYTES) + uint64_t(B200FA_WS_TRACE_BYTES) * B200FA_MAX_CTAS;
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 || ws_bytes < ws_need)
+    return fail(B200FA_ERR_WORKSPACE, "workspace must be 256-byte aligned and at least %llu bytes",
+                (unsigned long long)ws_need);
+  b200fa_options o_default{sizeof(b200fa_options), 0u, 0u, 0};
+  if (opts == nullptr) opts = &o_default;
+  if (opts->struct_size != sizeof(b200fa_options)) return fail(B200FA_ERR_OPTIONS, "b200fa_options.struct_size mismatch");
+  const int64_t nqb = ceil_div<int64_t>(Nq, kBlockM);
+  const int64_t items = plan_count<int64_t>(nqb, unit_begin, unit_end);
+  if (items == 0) return B200FA_OK;  // empty shard: nothing to launch
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int sms = 0;
+  rc = device_setup(dev, &sms);
+  if (rc != B200FA_OK) return rc;
+
+  FwdParams p;
+  std::memset(&p, 0, sizeof(p));
+  if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq)) != B200FA_OK) return rc;
+  p.Hq = int32_t(Hq);
+  p.Hkv = int32_t(Hkv);
+  p.group = int32_t(Hq / Hkv);
+  p.nqb = int32_t(nqb);
+  p.n_kv = int32_t(ceil_div<int64_t>(Nk, kBlockN));
+  p.nk_tail = int32_t(Nk - int64_t(p.n_kv - 1) * kBlockN);
+  p.unit_begin = int32_t(unit_begin);
+  p.unit_end = int32_t(unit_end);
+  p.num_items = int32_t(items);
+  p.scale_log2 = float(double(scale) * 1.4426950408889634074);
+  p.flags = opts->flags;
+  p.timeout_ns = uint64_t(opts->timeout_us ? opts->timeout_us : 2000000u) * 1000ull;
+  p.ws = static_cast<uint32_t*>(workspace);
+
+  int grid = sms;
+  if (opts->max_ctas > 0 && opts->max_ctas < grid) grid = opts->max_ctas;
+  if (grid > B200FA_MAX_CTAS) grid = B200FA_MAX_CTAS;
+  if (items < grid) grid = int(items);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (variant == B200FA_VARIANT_FP16)
+    b200_fa_fp16_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
+  else
+    b200_fa_fp32_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  return B200FA_OK;
+}
+
+int b200fa_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq,
+               int64_t Nk, int64_t D, float scale, int32_t variant, int64_t unit_begin, int64_t unit_end,
+               void* workspace, uint64_t ws_bytes, void* stream) {
+  return b200fa_fwd_ex(q, k, v, o, B, Hq, Hkv, Nq, Nk, D, scale, variant, unit_begin, unit_end, workspace, ws_bytes,
+                       stream, nullptr);
+}
+
+int b200fa_read_status(const void* workspace, void* stream, uint32_t* status) {
+  if (!workspace || !status) return fail(B200FA_ERR_NULL, "workspace and status must not be NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  e = cudaMemcpy(status, workspace, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy status");
+  return B200FA_OK;
+}
+
+int b200fa_reset_status(void* workspace, void* stream) {
+  if (!workspace) return fail(B200FA_ERR_NULL, "workspace must not be NULL");
+  const cudaError_t e = cudaMemsetAsync(workspace, 0, B200FA_WS_HEADER_BYTES, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync status");
+  return B200FA_OK;
+}
+
+const char* b200fa_kernel_name(int32_t variant) {
+  if (variant == B200FA_VARIANT_FP16) return "b200_fa_fp16_kernel";
+  if (variant == B200FA_VARIANT_FP32) return "b200_fa_fp32_kernel";
+  return nullptr;
+}
+
+const char* b200fa_last_error_string(void) { return g_last_error; }
+
+const char* b200fa_version(void) { return "b200fa 0.1 sm_100a"; }
+
+}  // extern "C"

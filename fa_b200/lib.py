@@ -1,0 +1,159 @@
+"""ctypes binding of ``libb200fa.so`` (the C ABI of include/b200fa.h).
+
+This module is the Python equivalent of the reference CCE binding's native
+half (backends/cce_fa_*/binding.py:7-31: ``CDLL`` of the operator library,
+``argtypes``/``restype`` declarations, nonzero status -> ``RuntimeError``).
+No torch types cross the boundary: only integers, pointers and a float.
+
+There is no fallback: if the library cannot be built or loaded the calls
+raise.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import threading
+
+from . import build as _build
+
+VARIANT_FP16 = 0
+VARIANT_FP32 = 1
+VARIANTS = {"fp16": VARIANT_FP16, "fp32": VARIANT_FP32}
+
+FLAG_TRACE = 1
+FLAG_TEST_WITHHOLD_P = 2
+
+DEV_OK = 0
+DEV_TIMEOUT = 1
+
+WS_HEADER_BYTES = 256
+WS_TRACE_BYTES = 32
+MAX_CTAS = 1024
+
+# name -> (restype, argtypes); the exported C ABI, one entry per declaration
+# of include/b200fa.h.
+_i64, _i32, _u32, _u64, _p, _f = C.c_int64, C.c_int32, C.c_uint32, C.c_uint64, C.c_void_p, C.c_float
+
+
+class Options(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("flags", C.c_uint32),
+                ("timeout_us", C.c_uint32), ("max_ctas", C.c_int32)]
+
+
+SIGNATURES = {
+    "b200fa_num_units": (_i64, [_i64, _i64, _i64]),
+    "b200fa_partition": (C.c_int, [_i64, _i32, _i32, C.POINTER(_i64), C.POINTER(_i64)]),
+    "b200fa_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _i64, _i64, _i32]),
+    "b200fa_fwd": (C.c_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i32,
+                             _i64, _i64, _p, _u64, _p]),
+    "b200fa_fwd_ex": (C.c_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i32,
+                                _i64, _i64, _p, _u64, _p, C.POINTER(Options)]),
+    "b200fa_read_status": (C.c_int, [_p, _p, C.POINTER(_u32)]),
+    "b200fa_reset_status": (C.c_int, [_p, _p]),
+    "b200fa_kernel_name": (C.c_char_p, [_i32]),
+    "b200fa_plan_item": (_i64, [_i64, _i64, _i64, _i64, _i64, _i64,
+                                C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]),
+    "b200fa_last_error_string": (C.c_char_p, []),
+    "b200fa_version": (C.c_char_p, []),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class B200FAError(RuntimeError):
+    """A nonzero status from libb200fa (negative: validation, positive: CUDA)."""
+
+    def __init__(self, where, status, message):
+        super().__init__(f"{where}: status {status}: {message}")
+        self.status = status
+
+
+def load(build_if_needed: bool = True) -> C.CDLL:
+    """Load (building first if the sources changed) and bind the library."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if build_if_needed:
+            path = _build.build()
+        else:
+            path = _build.LIB_PATH
+            if not path.is_file():
+                raise FileNotFoundError(f"{path} is not built; run fa_b200.build.build()")
+        lib = C.CDLL(str(path), mode=C.RTLD_LOCAL)
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return load().b200fa_last_error_string().decode()
+
+
+def check(status: int, where: str) -> None:
+    if status != 0:
+        raise B200FAError(where, status, last_error())
+
+
+def num_units(B: int, Hq: int, Nq: int) -> int:
+    n = load().b200fa_num_units(B, Hq, Nq)
+    if n < 0:
+        check(int(n), "b200fa_num_units")
+    return int(n)
+
+
+def partition(total: int, parts: int, index: int) -> tuple[int, int]:
+    b, e = _i64(), _i64()
+    check(load().b200fa_partition(total, parts, index, C.byref(b), C.byref(e)), "b200fa_partition")
+    return b.value, e.value
+
+
+def workspace_size(B, Hq, Hkv, Nq, Nk, D, variant) -> int:
+    n = load().b200fa_workspace_size(B, Hq, Hkv, Nq, Nk, D, variant)
+    if n < 0:
+        check(int(n), "b200fa_workspace_size")
+    return int(n)
+
+
+def plan_items(B, Hq, Nq, unit_begin, unit_end) -> list[tuple[int, int, int]]:
+    """Host-side work-item plan of a unit range: [(bh, first q-block, count)]."""
+    lib = load()
+    bh, qb, cnt = _i64(), _i64(), _i64()
+    n = lib.b200fa_plan_item(B, Hq, Nq, unit_begin, unit_end, -1, None, None, None)
+    if n < 0:
+        check(int(n), "b200fa_plan_item")
+    out = []
+    for i in range(n):
+        lib.b200fa_plan_item(B, Hq, Nq, unit_begin, unit_end, i, C.byref(bh), C.byref(qb), C.byref(cnt))
+        out.append((bh.value, qb.value, cnt.value))
+    return out
+
+
+def kernel_name(variant: int) -> str:
+    name = load().b200fa_kernel_name(variant)
+    if name is None:
+        raise ValueError(f"unknown variant {variant}")
+    return name.decode()
+
+
+def fwd(q_ptr, k_ptr, v_ptr, o_ptr, B, Hq, Hkv, Nq, Nk, D, scale, variant,
+        unit_begin, unit_end, ws_ptr, ws_bytes, stream, *, flags=0, timeout_us=0, max_ctas=0):
+    """Raw pointer call of b200fa_fwd_ex; raises B200FAError on a nonzero status."""
+    opts = Options(C.sizeof(Options), flags, timeout_us, max_ctas)
+    status = load().b200fa_fwd_ex(q_ptr, k_ptr, v_ptr, o_ptr, B, Hq, Hkv, Nq, Nk, D, scale, variant,
+                                  unit_begin, unit_end, ws_ptr, ws_bytes, stream, C.byref(opts))
+    check(status, "b200fa_fwd")
+
+
+def read_status(ws_ptr, stream) -> tuple[int, int, int, int]:
+    out = (_u32 * 4)()
+    check(load().b200fa_read_status(ws_ptr, stream, out), "b200fa_read_status")
+    return tuple(int(x) for x in out)
+
+
+def reset_status(ws_ptr, stream) -> None:
+    check(load().b200fa_reset_status(ws_ptr, stream), "b200fa_reset_status")

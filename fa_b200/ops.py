@@ -1,0 +1,142 @@
+"""Torch-facing attention operator over ``libb200fa.so``.
+
+``Operator`` is the B200 counterpart of the reference CCE binding's
+``Operator`` (backends/cce_fa_nqkq_nz_resident_v13_q768_pool_i4_p128/
+binding.py:139-242): same call signature ``op(q, k, v) -> O``, same argument
+checks and ``ValueError`` messages (binding.py:219-231), workspace owned and
+reused by the operator (binding.py:166-187, 208-209).  Differences, all
+relaxations: any Nq >= 1 and Nk >= 1 is accepted (the reference requires
+Nq % 128 == 0 and Nk % 512 == 0), and a unit range selects a shard of the
+(b, hq, 128-row query block) grid for multi-GPU runs.
+
+PyTorch is used for device memory and streams only; all arithmetic runs in
+the sm_100a kernels.  There is no CPU or eager fallback: a missing library or
+a non-CUDA tensor raises.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import lib
+
+HEAD_DIM = 128
+BLOCK_M = 128
+
+
+def _geometry(q, k, v):
+    """Validate like binding.py:219-231 and return (B, Hq, Hkv, Nq, Nk)."""
+    if q.ndim != 4 or k.ndim != 4 or v.shape != k.shape:
+        raise ValueError("Q/K/V must be [B,H,N,128]")
+    b, h, nq, d = q.shape
+    if (min(q.shape) <= 0 or min(k.shape) <= 0 or k.shape[0] != b or d != HEAD_DIM
+            or k.shape[3] != HEAD_DIM or h % k.shape[1]):
+        raise ValueError("invalid attention geometry")
+    nk = k.shape[2]
+    if max(nq, nk) > 2**31 - 1:
+        raise ValueError("unsupported query/key tail")
+    for t in (q, k, v):
+        if (t.device.type != "cuda" or t.device != q.device or t.dtype != torch.float16
+                or not t.is_contiguous()):
+            raise ValueError("Q/K/V must be contiguous FP16 on the same CUDA device")
+    return b, h, k.shape[1], nq, nk
+
+
+class Operator:
+    """``op(q, k, v) -> O``: non-causal GQA attention forward, FP16 in/out.
+
+    variant: "fp16" (FP16 exp/partial sums, the CCE FP16 kernel's numerics)
+             or "fp32" (FP32 softmax, the CCE FP32 kernel's numerics).
+    """
+
+    def __init__(self, variant: str = "fp16", *, timeout_us: int = 0, trace: bool = False,
+                 max_ctas: int = 0):
+        if variant not in lib.VARIANTS:
+            raise ValueError(f"variant must be one of {sorted(lib.VARIANTS)}")
+        self.variant = variant
+        self.variant_id = lib.VARIANTS[variant]
+        self.timeout_us = int(timeout_us)
+        self.flags = lib.FLAG_TRACE if trace else 0
+        self.max_ctas = int(max_ctas)
+        self.workspaces = {}  # device -> uint8 tensor (zeroed once)
+        lib.load()
+
+    @property
+    def kernel_name(self) -> str:
+        return lib.kernel_name(self.variant_id)
+
+    def workspace(self, device) -> torch.Tensor:
+        ws = self.workspaces.get(device)
+        if ws is None:
+            nbytes = lib.WS_HEADER_BYTES + lib.WS_TRACE_BYTES * lib.MAX_CTAS
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+            self.workspaces[device] = ws
+        return ws
+
+    def __call__(self, q, k, v, *, scale: float | None = None, out: torch.Tensor | None = None,
+                 unit_range: tuple[int, int] | None = None, flags: int = 0) -> torch.Tensor:
+        B, Hq, Hkv, Nq, Nk = _geometry(q, k, v)
+        if out is None:
+            out = torch.empty_like(q)
+        elif out.shape != q.shape or out.dtype != torch.float16 or not out.is_contiguous() \
+                or out.device != q.device:
+            raise ValueError("out must be a contiguous FP16 tensor shaped like Q on Q's device")
+        units = lib.num_units(B, Hq, Nq)
+        begin, end = (0, units) if unit_range is None else (int(unit_range[0]), int(unit_range[1]))
+        scale = float(HEAD_DIM ** -0.5 if scale is None else scale)
+        ws = self.workspace(q.device)
+        with torch.cuda.device(q.device):
+            stream = torch.cuda.current_stream(q.device).cuda_stream
+            lib.fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                    B, Hq, Hkv, Nq, Nk, HEAD_DIM, scale, self.variant_id, begin, end,
+                    ws.data_ptr(), ws.numel(), stream,
+                    flags=self.flags | flags, timeout_us=self.timeout_us, max_ctas=self.max_ctas)
+        return out
+
+    def status(self, device) -> tuple[int, int, int, int]:
+        """Synchronize and read the device status header {status, site, cta, 0}."""
+        ws = self.workspace(torch.device(device))
+        with torch.cuda.device(ws.device):
+            return lib.read_status(ws.data_ptr(), torch.cuda.current_stream(ws.device).cuda_stream)
+
+    def reset_status(self, device) -> None:
+        ws = self.workspace(torch.device(device))
+        with torch.cuda.device(ws.device):
+            lib.reset_status(ws.data_ptr(), torch.cuda.current_stream(ws.device).cuda_stream)
+
+    def trace(self, device) -> list[dict]:
+        """Per-CTA trace records of the last traced call (synchronizes)."""
+        ws = self.workspace(torch.device(device))
+        torch.cuda.synchronize(ws.device)
+        raw = ws[lib.WS_HEADER_BYTES:].view(torch.int32).view(-1, 8).cpu()
+        recs = []
+        for r in raw.tolist():
+            t0 = (r[2] & 0xFFFFFFFF) | ((r[3] & 0xFFFFFFFF) << 32)
+            t1 = (r[4] & 0xFFFFFFFF) | ((r[5] & 0xFFFFFFFF) << 32)
+            if t1 == 0:
+                continue
+            recs.append({"smid": r[0], "items": r[1], "t_start_ns": t0, "t_end_ns": t1})
+        return recs
+
+
+_OPS = {}
+
+
+def attention(q, k, v, *, variant: str = "fp16", scale: float | None = None, out=None,
+              unit_range=None) -> torch.Tensor:
+    """Functional form: O = softmax(Q K^T * scale) V with GQA (Hq % Hkv == 0)."""
+    op = _OPS.get(variant)
+    if op is None:
+        op = _OPS[variant] = Operator(variant)
+    return op(q, k, v, scale=scale, out=out, unit_range=unit_range)
+
+
+def flops(B: int, Hq: int, Nq: int, Nk: int, D: int = HEAD_DIM) -> int:
+    """QK^T and PV FLOPs, 4*B*Hq*Nq*Nk*D (reference README.md:86)."""
+    return 4 * B * Hq * Nq * Nk * D
+
+
+def num_units(B: int, Hq: int, Nq: int) -> int:
+    return B * Hq * math.ceil(Nq / BLOCK_M)

@@ -1,0 +1,167 @@
+/*
+ * b200fa.h -- C ABI of libb200fa.so, the sm_100a flash-attention forward.
+ *
+ * One operator: non-causal grouped-query attention forward,
+ *     O[b,h] = softmax(Q[b,h] K[b,kv(h)]^T * scale) V[b,kv(h)],
+ *     kv(h) = h / (Hq / Hkv),
+ * with FP16 Q [B,Hq,Nq,128], K and V [B,Hkv,Nk,128] and FP16 normalized
+ * O [B,Hq,Nq,128], all contiguous (BHND, "BNSD" in torch_npu terms).
+ *
+ * This library replaces the native call pair of the reference's CCE
+ * backends,
+ *   aclnn<Op>GetWorkspaceSize(q, k, v, q_block, k_block, q_l1, groups,
+ *                             capture, phase, [gray], sp, partial, trace,
+ *                             stats, running, output, &ws_size, &executor)
+ *   aclnn<Op>(workspace, ws_size, executor, stream)
+ * bound in backends/cce_fa_nqkq_nz_resident_v13_q768_pool_i4_p128/binding.py:20-26
+ * and called at binding.py:72-80 (the FP32 twin,
+ * backends/cce_fa_nk_nz_vector_fp32_v5_sumpack/binding.py, has the same
+ * shape).  The ACLNN executor and its tiling (op_host/*.cpp:53-89) collapse
+ * into the plain-pointer call b200fa_fwd below; the host-side shape checks of
+ * binding.py:87-98 and op_host/*.cpp:8-19 become the negative return codes.
+ *
+ * Conventions
+ *   - All tensor pointers are CUDA device pointers owned by the caller; the
+ *     library allocates no device memory and keeps no per-call state.
+ *   - Calls are asynchronous on the caller's stream (cudaStream_t passed as
+ *     void*, NULL = legacy default stream); nothing synchronizes implicitly
+ *     except b200fa_read_status.
+ *   - Return value 0 = success, negative = argument validation error (no
+ *     CUDA call was made), positive = CUDA runtime error code from a launch
+ *     or attribute call.  b200fa_last_error_string() describes the last
+ *     failure on the calling thread.
+ *   - Device-side failures (a bounded wait that ran out) do not abort the
+ *     kernel's caller: the kernel records a status word in the workspace
+ *     and returns; b200fa_read_status() reads it.
+ */
+#ifndef B200FA_H_
+#define B200FA_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Variant selector: softmax arithmetic of the two shipped kernels.
+ * B200FA_VARIANT_FP16 mirrors the reference CCE FP16 kernel
+ *   (backends/cce_fa_nqkq_nz_resident_v13_q768_pool_i4_p128): FP16 exponent
+ *   arguments, FP16 exp2 and FP16 partial row sums.
+ * B200FA_VARIANT_FP32 mirrors the CCE FP32 kernel
+ *   (backends/cce_fa_nk_nz_vector_fp32_v5_sumpack): FP32 softmax throughout.
+ * Both keep P in FP16 for the tensor-core PV product and accumulate O in
+ * FP32 in tensor memory. */
+#define B200FA_VARIANT_FP16 0
+#define B200FA_VARIANT_FP32 1
+
+/* Status / error codes. */
+#define B200FA_OK                 0
+#define B200FA_ERR_NULL          -1   /* a required pointer is NULL            */
+#define B200FA_ERR_HEAD_DIM      -2   /* D != 128                              */
+#define B200FA_ERR_SHAPE         -3   /* B, Hq, Hkv, Nq or Nk <= 0             */
+#define B200FA_ERR_GROUPING      -4   /* Hq % Hkv != 0                         */
+#define B200FA_ERR_TOO_LARGE     -5   /* Nq, Nk or unit count >= 2^31          */
+#define B200FA_ERR_UNIT_RANGE    -6   /* unit range outside [0, num_units]     */
+#define B200FA_ERR_ALIGNMENT     -7   /* a tensor pointer is not 16-B aligned  */
+#define B200FA_ERR_WORKSPACE     -8   /* workspace NULL, misaligned or small   */
+#define B200FA_ERR_VARIANT       -9   /* unknown variant                       */
+#define B200FA_ERR_SCALE        -10   /* scale not finite or not positive      */
+#define B200FA_ERR_OPTIONS      -11   /* malformed b200fa_options              */
+#define B200FA_ERR_NO_DRIVER    -12   /* cuTensorMapEncodeTiled unavailable    */
+#define B200FA_ERR_TENSOR_MAP   -13   /* cuTensorMapEncodeTiled rejected a map */
+
+/* Device status word values (b200fa_read_status, status[0]). */
+#define B200FA_DEV_OK             0
+#define B200FA_DEV_TIMEOUT        1   /* a bounded mbarrier wait ran out       */
+
+/* Option flags (b200fa_options.flags). */
+#define B200FA_FLAG_TRACE          1u /* write one trace record per CTA        */
+/* Test-only: softmax warpgroup 1 withholds its first P-ready arrival, so the
+ * MMA warp's bounded wait runs out and the kernel reports
+ * B200FA_DEV_TIMEOUT.  Used by the failure-detection test only. */
+#define B200FA_FLAG_TEST_WITHHOLD_P 2u
+
+typedef struct b200fa_options {
+    uint32_t struct_size;   /* sizeof(b200fa_options)                        */
+    uint32_t flags;         /* B200FA_FLAG_*                                  */
+    uint32_t timeout_us;    /* bound of every device-side wait; 0 = 2 s       */
+    int32_t  max_ctas;      /* cap on the persistent grid; <= 0 = one per SM  */
+} b200fa_options;
+
+/* Workspace layout (bytes, 256-B aligned, zeroed once by the owner):
+ *   [0, 256)       status header: u32 status, u32 site, u32 cta, u32 spare...
+ *   [256, ...)     trace records, one per CTA (B200FA_FLAG_TRACE):
+ *                  {u32 smid, u32 items, u64 t_start_ns, u64 t_end_ns, u64 0}
+ * The status is sticky: it stays set until b200fa_reset_status. */
+#define B200FA_WS_HEADER_BYTES 256u
+#define B200FA_WS_TRACE_BYTES   32u
+#define B200FA_MAX_CTAS       1024
+
+/* Number of work units: (b, hq, 128-row query block) triples, linearised as
+ * ((b * Hq) + hq) * ceil(Nq / 128) + qb -- the order of the reference's
+ * task split, cce_task.h:28-35 / panel_kernel.h:264-274.  Returns a negative
+ * validation code for non-positive sizes. */
+int64_t b200fa_num_units(int64_t B, int64_t Hq, int64_t Nq);
+
+/* Contiguous near-equal split of [0, total) into `parts` ranges, remainder to
+ * the first parts -- the semantics of cce::PartitionContiguous
+ * (cce_task.h:28-35).  Writes part `index`'s [begin, end).  0 or
+ * B200FA_ERR_UNIT_RANGE. */
+int b200fa_partition(int64_t total, int32_t parts, int32_t index,
+                     int64_t* begin, int64_t* end);
+
+/* Bytes of workspace b200fa_fwd needs (header + trace area for the maximum
+ * grid).  Replaces aclnn<Op>GetWorkspaceSize (binding.py:72-77); the value
+ * does not depend on the shape beyond validation.  Negative on invalid
+ * arguments. */
+int64_t b200fa_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq,
+                              int64_t Nk, int64_t D, int32_t variant);
+
+/* Attention forward over work units [unit_begin, unit_end) (the whole
+ * problem is [0, b200fa_num_units(B, Hq, Nq))).  Rows of O outside the range
+ * are not written.  Replaces aclnn<Op> (binding.py:72-80) and the tiling
+ * kernel launch (op_host/*.cpp:53-89, panel_kernel.h:216-343). */
+int b200fa_fwd(const void* q, const void* k, const void* v, void* o,
+               int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, int64_t Nk,
+               int64_t D, float scale, int32_t variant,
+               int64_t unit_begin, int64_t unit_end,
+               void* workspace, uint64_t ws_bytes, void* stream);
+
+/* b200fa_fwd with options (trace records, wait bound, grid cap, test
+ * flags).  opts may be NULL. */
+int b200fa_fwd_ex(const void* q, const void* k, const void* v, void* o,
+                  int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, int64_t Nk,
+                  int64_t D, float scale, int32_t variant,
+                  int64_t unit_begin, int64_t unit_end,
+                  void* workspace, uint64_t ws_bytes, void* stream,
+                  const b200fa_options* opts);
+
+/* Synchronizes `stream`, then copies the 4-word status header of `workspace`
+ * into status[0..3] = {status, site, cta, spare}.  Returns 0 or a CUDA error. */
+int b200fa_read_status(const void* workspace, void* stream, uint32_t* status);
+
+/* Clears the status header (async on `stream`). */
+int b200fa_reset_status(void* workspace, void* stream);
+
+/* Kernel symbol of a variant ("b200_fa_fp16_kernel" / "b200_fa_fp32_kernel"),
+ * the names the harness profiler matches backends by; NULL for a bad id. */
+const char* b200fa_kernel_name(int32_t variant);
+
+/* Host-side work-item plan (no GPU): item `index` of the range
+ * [unit_begin, unit_end) as {bh, first q-block, count (1 or 2)}.  Returns
+ * the number of items, or a negative code. */
+int64_t b200fa_plan_item(int64_t B, int64_t Hq, int64_t Nq,
+                         int64_t unit_begin, int64_t unit_end, int64_t index,
+                         int64_t* bh, int64_t* qblock, int64_t* count);
+
+/* Description of the last error on the calling thread ("" if none). */
+const char* b200fa_last_error_string(void);
+
+/* Library version string. */
+const char* b200fa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200FA_H_ */
