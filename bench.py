@@ -1,0 +1,397 @@
+"""Benchmark of the attention forward on B200: one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--variant fp16|fp32]
+                    [--impl b200|reference] [--shape B,Hq,Hkv,N]
+
+Workload: the BASELINE metric's configuration, B=2, Hq=12, Hkv=1,
+Nq=Nk=131072, D=128 (reference problem/cases.py CASES[0]), Q/K/V i.i.d.
+N(0,1) FP16 drawn on the device from seed 0 (synthetic, canonical.py
+semantics).  One step = one attention forward over the whole case; with N
+GPUs (torchrun, one rank per GPU) each rank runs its contiguous share of the
+(b, hq, 128-row q-block) units with K/V replicated (weak in the data, strong
+in the problem: the total work per step is fixed, so "scaling": "strong").
+
+Timing: W untimed warm-up steps, then K steps between a barrier and a
+device synchronize on both sides, CUDA events on the launching stream, max
+over ranks.  Inputs (805 MB of Q alone) are larger than the 126 MB L2, so no
+flush is needed between steps.
+
+Reported:
+  value       whole-job TFLOPS, 4*B*Hq*Nq*Nk*D / step time, inputs resident
+  e2e         the same metric through the public operator with host buffers:
+              per step each rank copies its Q rows and the full K/V from
+              pinned host memory, runs the kernel and copies its O rows back
+  roofline    tensor-bound: achieved TFLOP/s per kernel launch (CUDA events
+              around each launch) against the measured bf16 dense peak
+  cpu_baseline the oracle's FP32 PyTorch attention on the host cores over a
+              bounded sample (N=1, rank 0 only)
+  clocks      nvidia-smi samples taken during the timed region
+
+``--impl reference`` times the reference's CPU path instead (FP32 PyTorch
+attention, the formula of backends/expert_v2/impl_tl.py:701-717, restated in
+oracle/) on rank 0, each step a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "FA fwd TFLOPS & % of B200 FP16 tensor peak, B=2 N=131072, at 1/2/4/8 GPUs"
+NOMINAL_FP16_TFLOPS = 2250.0
+FALLBACK_TFLOPS = 1590.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--variant", choices=("fp16", "fp32"), default="fp16")
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--shape", type=str, default="2,12,1,131072",
+                   help="B,Hq,Hkv,N (default: the BASELINE metric config)")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", 0.0)), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_TFLOPS, 1400.0, "fallback"
+
+
+def load_traffic(workload):
+    """DRAM bytes per launch of the top kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d.get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms (rank 0)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(gpu_indices)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                idx = int(f[0])
+            except ValueError:
+                continue
+            if self.gpus and idx not in self.gpus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                pass
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
+
+
+def max_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_reference(args, B, Hq, Hkv, N):
+    """--impl reference: the reference CPU path (FP32 PyTorch attention) on rank 0."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+    from oracle.attention_ref import cpu_time_sample
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    # Size each step to ~2 s of CPU work from a short calibration run.
+    rate, el, reps, th, _ = cpu_time_sample(B, Hq, Hkv, N, rows=256, threads=threads)
+    flop_per_row = 4 * N * 128
+    rows = int(max(64, min(8192, (2.0 * rate * 1e12) / flop_per_row)))
+    rows -= rows % 64
+    for _ in range(args.warmup):
+        cpu_time_sample(B, Hq, Hkv, N, rows=rows, threads=threads)
+    t_total, fl_total = 0.0, 0
+    desc = ""
+    for _ in range(args.steps):
+        r, el, reps, th, desc = cpu_time_sample(B, Hq, Hkv, N, rows=rows, threads=threads)
+        t_total += el
+        fl_total += 4 * rows * N * 128 * reps
+    value = fl_total / t_total / 1e12
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "TFLOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * t_total / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic (seeded N(0,1) FP16 inputs, canonical.py semantics)",
+        "config": {"workload": f"B{B}_S{N}_Q{Hq}_KV{Hkv}_D128 attention forward (CPU sample)",
+                   "batch": B, "heads_q": Hq, "heads_kv": Hkv, "seq_len": N, "head_dim": 128},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOPS", "cores": th, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": round(value, 4), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    B, Hq, Hkv, N = (int(x) for x in args.shape.split(","))
+    if args.impl == "reference":
+        return run_reference(args, B, Hq, Hkv, N)
+
+    import torch
+
+    from fa_b200 import lib
+    from fa_b200.ops import Operator
+    from fa_b200.shard import num_units, partition, row_range
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    D = 128
+    flops_case = 4 * B * Hq * N * N * D
+    workload = f"B{B}_S{N}_Q{Hq}_KV{Hkv}_D128"
+
+    # Canonical inputs on the device (seeded, identical on every rank).
+    torch.manual_seed(args.seed)
+    q = torch.randn((B, Hq, N, D), dtype=torch.float16, device=dev)
+    k = torch.randn((B, Hkv, N, D), dtype=torch.float16, device=dev)
+    v = torch.randn((B, Hkv, N, D), dtype=torch.float16, device=dev)
+    o = torch.empty_like(q)
+    units = num_units(B, Hq, N)
+    ub, ue = partition(units, world, rank)
+    r0, r1 = row_range(ub, ue, N)
+    op = Operator(args.variant)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        op(q, k, v, out=o, unit_range=(ub, ue))
+
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    status = op.status(dev)
+    if status[0] != 0:
+        raise RuntimeError(f"device status {status} after warm-up")
+
+    sampler = ClockSampler(range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.4)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    t1.record(stream)
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    local_ms = t0.elapsed_time(t1)
+    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    total_ms = max_over_ranks(local_ms, world)
+    launch_ms_max = max_over_ranks(launch_ms, world)
+    status = op.status(dev)
+    if status[0] != 0:
+        raise RuntimeError(f"device status {status} after the timed region")
+    ms_per_step = total_ms / args.steps
+    value = flops_case / (ms_per_step * 1e-3) / 1e12
+
+    # End to end through the public operator with host buffers.
+    e2e = None
+    if not args.no_e2e:
+        qf = q.view(-1, D)
+        q_host = torch.empty((r1 - r0, D), dtype=torch.float16, pin_memory=True)
+        q_host.copy_(qf[r0:r1])
+        k_host = torch.empty(k.shape, dtype=k.dtype, pin_memory=True)
+        v_host = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
+        k_host.copy_(k)
+        v_host.copy_(v)
+        o_host = torch.empty((r1 - r0, D), dtype=torch.float16, pin_memory=True)
+        e2e_steps = max(1, min(args.steps, 5))
+
+        def e2e_step():
+            qf[r0:r1].copy_(q_host, non_blocking=True)
+            k.copy_(k_host, non_blocking=True)
+            v.copy_(v_host, non_blocking=True)
+            op(q, k, v, out=o, unit_range=(ub, ue))
+            o_host.copy_(o.view(-1, D)[r0:r1], non_blocking=True)
+
+        e2e_step()
+        barrier(world)
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        b_.record(stream)
+        barrier(world)
+        e2e_ms = max_over_ranks(a.elapsed_time(b_), world) / e2e_steps
+        h2d_local = (r1 - r0) * D * 2 + k.numel() * 2 + v.numel() * 2
+        d2h_local = (r1 - r0) * D * 2
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([h2d_local, d2h_local], dtype=torch.float64, device=dev)
+            dist.all_reduce(t)
+            h2d_local, d2h_local = int(t[0].item()), int(t[1].item())
+        e2e = {"value": round(flops_case / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+               "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d_local,
+               "d2h_bytes_per_step": d2h_local}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.attention_ref import cpu_time_sample
+
+        threads = os.cpu_count() or 1
+        rate, el, reps, th, _ = cpu_time_sample(B, Hq, Hkv, N, rows=256, threads=threads)
+        rows = int(max(64, min(8192, (args.cpu_seconds / 4) * rate * 1e12 / (4 * N * D))))
+        rows -= rows % 64
+        rate, el, reps, th, desc = cpu_time_sample(B, Hq, Hkv, N, rows=rows, threads=threads,
+                                                   min_seconds=args.cpu_seconds)
+        cpu = {"value": round(rate, 4), "unit": "TFLOPS", "cores": th, "kind": "port", "sample": desc}
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peak_burst, peak_sust, peak_kind = load_peaks()
+    flops_launch = 4 * (r1 - r0) * N * D  # this rank's units, rank 0's launch
+    achieved = flops_launch / (launch_ms * 1e-3) / 1e12
+    traffic = load_traffic(workload) if world == 1 else None
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "TFLOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp16",
+        "data": "synthetic (seeded N(0,1) FP16 Q/K/V on device, canonical.py semantics)",
+        "config": {
+            "workload": f"{workload} non-causal GQA attention forward, {args.variant} variant",
+            "batch": B, "heads_q": Hq, "heads_kv": Hkv, "seq_len": N, "head_dim": 128,
+            "variant": args.variant, "kernel": op.kernel_name,
+            "parallelism": f"q-block shards x{world}, K/V replicated",
+            "l2": "inputs larger than L2 (Q 805 MB), no flush",
+        },
+        "pct_peak": round(value / (peak_burst * world), 4),
+        "pct_nominal_fp16_peak": round(value / (NOMINAL_FP16_TFLOPS * world), 4),
+        "roofline": {
+            "bound": "tensor",
+            "achieved": round(achieved, 2),
+            "peak": peak_burst,
+            "unit": "TFLOP/s",
+            "frac": round(achieved / peak_burst, 4),
+            "peak_kind": f"{peak_kind} bf16 dense burst (sustained {peak_sust})",
+            "traffic": traffic,
+            "launch_ms": round(launch_ms, 3),
+            "launch_ms_max_rank": round(launch_ms_max, 3),
+        },
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "device_status": list(status),
+        "library": str(lib.load()._name),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

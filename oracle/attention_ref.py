@@ -19,6 +19,9 @@ What it restates
   the most exact statement of the operator, used to pin the FP32 one.
 * ``attention_rows_fp32`` -- selected query rows only, for spot checks of
   full-size problems.
+* ``attention_sdpa_fp32`` -- the reference formula in its own form
+  (repeat_interleave + FP32 ``scaled_dot_product_attention``): the CPU path
+  that bench.py times as the CPU baseline.
 
 Pinning
 -------
@@ -124,12 +127,26 @@ def flops(B: int, Hq: int, Nq: int, Nk: int, D: int = 128) -> int:
     return 4 * B * Hq * Nq * Nk * D
 
 
+def attention_sdpa_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """The reference formula verbatim in structure (impl_tl.py:701-717): GQA by
+    repeat_interleave, FP32 scaled_dot_product_attention, default scale,
+    non-causal; FP32 result (before the reference's FP16 cast).  This is the
+    reference's CPU path that the CPU baseline times."""
+    if k.shape[1] != q.shape[1]:
+        rep = q.shape[1] // k.shape[1]
+        k = k.repeat_interleave(rep, dim=1)
+        v = v.repeat_interleave(rep, dim=1)
+    return torch.nn.functional.scaled_dot_product_attention(
+        q.float(), k.float(), v.float(), attn_mask=None, dropout_p=0.0, is_causal=False)
+
+
 def cpu_time_sample(B: int, Hq: int, Hkv: int, N: int, rows: int, seed: int = 0,
                     threads: int | None = None, min_seconds: float = 0.0):
-    """Time ``attention_fp32`` on the host cores over a bounded sample of a case.
+    """Time the reference's CPU path (``attention_sdpa_fp32``) on the host cores
+    over a bounded sample of a case.
 
     The sample is ``rows`` query rows of one (b, h) against the full Nk keys;
-    the work is linear in Nq, so throughput scales to the whole case.
+    the work is linear in Nq, so throughput carries over to the whole case.
     Repeats until ``min_seconds`` elapsed.  Returns (tflops, seconds, reps,
     threads, sample description).
     """
@@ -141,20 +158,20 @@ def cpu_time_sample(B: int, Hq: int, Hkv: int, N: int, rows: int, seed: int = 0,
     q = torch.randn((1, 1, rows, 128), generator=g).half()
     k = torch.randn((1, 1, N, 128), generator=g).half()
     v = torch.randn((1, 1, N, 128), generator=g).half()
-    attention_fp32(q, k, v, rows_per_block=min(rows, 256))  # warm-up
+    attention_sdpa_fp32(q, k, v)  # warm-up
     reps, t0 = 0, time.perf_counter()
     while True:
-        attention_fp32(q, k, v, rows_per_block=min(rows, 256))
+        attention_sdpa_fp32(q, k, v)
         reps += 1
         el = time.perf_counter() - t0
         if el >= min_seconds:
             break
     fl = flops(1, 1, rows, N) * reps
-    desc = (f"{rows} query rows x 1 head x Nk={N} keys (of B={B},Hq={Hq},Hkv={Hkv},N={N}), "
-            f"{reps} reps, scaled linearly in Nq")
+    desc = (f"{rows} query rows x 1 head x Nk={N} keys of B={B},Hq={Hq},Hkv={Hkv},N={N} "
+            f"(FP32 scaled_dot_product_attention, {reps} reps), throughput scaled linearly in Nq")
     return fl / el / 1e12, el, reps, torch.get_num_threads(), desc
 
 
-__all__ = ["attention_fp32", "attention_rows_fp32", "attention_f64", "to_fp16", "errors", "flops",
-           "cpu_time_sample"]
+__all__ = ["attention_fp32", "attention_sdpa_fp32", "attention_rows_fp32", "attention_f64", "to_fp16",
+           "errors", "flops", "cpu_time_sample"]
 

@@ -1,0 +1,104 @@
+"""The oracle pinned to the reference's own code (CPU only).
+
+tests/golden/ was produced by running the reference's ``ref_flash_attn``
+(backends/expert_v2/impl_tl.py:701-717), ``Case`` (problem/cases.py) and
+``build_canonical`` (problem/canonical.py, NPU redirected to CPU) in the
+build container (tests/golden/make_golden.py).  These tests check that the
+oracle's restatements and the harness mirror reproduce those results.
+"""
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.attention_ref import attention_f64, attention_fp32, attention_rows_fp32, attention_sdpa_fp32
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+META = json.loads((GOLDEN / "cases.json").read_text())
+VECTORS = np.load(GOLDEN / "attention_vectors.npz")
+
+
+def _fp16_half_ulp(x: np.ndarray) -> np.ndarray:
+    """Half a unit in the last place of FP16 at |x| (the reference's final cast)."""
+    ax = np.maximum(np.abs(x), 2.0 ** -14)
+    return 2.0 ** (np.floor(np.log2(ax)) - 11)
+
+
+def _slack(i):
+    """Allowed FP32-accumulation difference beyond the FP16 rounding.
+
+    N(0,1) inputs: 2e-6.  Large-magnitude inputs (peaked softmax, logits ~60):
+    the reference's own FP32 dot products carry ~1e-5 relative error, which
+    moves the weights of near-tied top keys by ~1e-3 -- the reference itself
+    is only that accurate there, so the pin uses the acceptance bar, 2e-3.
+    """
+    return 2e-6 if META["vectors"][i]["input_scale"] == 1.0 else 2e-3
+
+
+@pytest.mark.parametrize("i", range(len(META["vectors"])))
+def test_fp64_restatement_matches_reference_vectors(i):
+    q, k, v, o = (VECTORS[f"{n}{i}"] for n in "qkvo")
+    ref = attention_f64(q, k, v)
+    # The reference rounds an FP32 result to FP16: allow that rounding plus the
+    # FP32 accumulation difference.
+    err = np.abs(ref - o.astype(np.float64))
+    assert (err <= _fp16_half_ulp(ref) + _slack(i)).all(), float(err.max())
+
+
+@pytest.mark.parametrize("i", range(len(META["vectors"])))
+def test_fp32_restatement_matches_reference_vectors(i):
+    q, k, v, o = (torch.from_numpy(VECTORS[f"{n}{i}"]) for n in "qkvo")
+    out = attention_fp32(q, k, v, rows_per_block=64)
+    err = (out.double() - o.double()).abs().numpy()
+    assert (err <= _fp16_half_ulp(out.double().numpy()) + _slack(i)).all(), float(err.max())
+    # SDPA form (what the CPU baseline times) agrees too.
+    sd = attention_sdpa_fp32(q, k, v)
+    assert (sd - out).abs().max() < max(1e-5, _slack(i))
+
+
+def test_row_sampler_matches_full_oracle():
+    q, k, v = (torch.from_numpy(VECTORS[f"{n}1"]) for n in "qkv")
+    full = attention_fp32(q, k, v)
+    rows = torch.tensor([[0, 0, 0], [0, 3, 127], [0, 1, 64], [0, 2, 5]])
+    part = attention_rows_fp32(q, k, v, rows)
+    for j, (b, h, r) in enumerate(rows.tolist()):
+        assert (part[j] - full[b, h, r]).abs().max() < 1e-5
+
+
+def test_vectors_cover_edge_cases():
+    vecs = META["vectors"]
+    assert any(v["Nq"] % 128 for v in vecs), "query tail"
+    assert any(v["Nk"] % 128 for v in vecs), "key tail"
+    assert any(v["Nq"] != v["Nk"] for v in vecs), "Nq != Nk"
+    assert any(v["Hq"] != v["Hkv"] for v in vecs) and any(v["Hq"] == v["Hkv"] for v in vecs)
+    assert any(v["input_scale"] > 1 for v in vecs), "large magnitude"
+    assert any(v["Nk"] <= 128 for v in vecs), "single key block"
+
+
+def test_cases_mirror_reference():
+    from fa_b200.problem.cases import CASES, Case
+
+    for i, rc in enumerate(META["reference_cases"]):
+        c = CASES[i]  # indices 0-2 keep the reference's meaning
+        assert (c.batch, c.seq_len, c.heads_q, c.heads_kv, c.dim) == (
+            rc["batch"], rc["seq_len"], rc["heads_q"], rc["heads_kv"], rc["dim"])
+        assert c.name == rc["name"] and c.scale == rc["scale"] and c.group_size == rc["group_size"]
+    for rc in META["baseline_cases"]:
+        c = Case(rc["batch"], rc["seq_len"], rc["heads_q"], rc["heads_kv"], rc["dim"])
+        assert c in CASES and c.name == rc["name"] and c.scale == rc["scale"]
+
+
+def test_canonical_inputs_match_reference_generator_on_cpu():
+    from fa_b200.problem.canonical import build_canonical
+    from fa_b200.problem.cases import Case
+
+    for chk in META["canonical_checks"]:
+        t = build_canonical(Case(*chk["case"]), chk["seed"], device="cpu")
+        for n in "qkv":
+            assert list(t[n].shape) == chk[f"{n}_shape"]
+            assert t[n].dtype == torch.float16
+            assert float(t[n].double().sum()) == chk[f"{n}_sum"]
+            assert [float(x) for x in t[n].flatten()[:4]] == chk[f"{n}_head"]
