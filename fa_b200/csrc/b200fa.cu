@@ -260,3 +260,115 @@ const char* b200fa_last_error_string(void) { return g_last_error; }
 const char* b200fa_version(void) { return "b200fa 0.1 sm_100a"; }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point (b200fa_fwd_noalloc).  For callers that cannot
+// hand the library a workspace -- a C/FFI host without a device allocator, a
+// runtime that owns the whole device pool, a path that must not call
+// cudaMalloc because it can synchronize the device.  The kernel's scratch
+// (status header + trace records) lives in this file-scope device array
+// instead: one copy per device that loads the library, kept until exit.
+namespace {
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[B200FA_NOALLOC_SCRATCH_BYTES];
+
+struct NoAllocScratch {
+  std::once_flag once;
+  void* ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+NoAllocScratch g_noalloc[64];
+
+// Device address of device `dev`'s copy of g_noalloc_scratch.  In host code
+// the array's name is only a host-side stand-in, so the address is resolved
+// once per device, with that device current, and cached.
+int noalloc_scratch(int dev, void** out) {
+  if (dev < 0 || dev >= 64) return fail(B200FA_ERR_OPTIONS, "device ordinal %d out of range", dev);
+  NoAllocScratch& s = g_noalloc[dev];
+  std::call_once(s.once, [&s] { s.err = cudaGetSymbolAddress(&s.ptr, g_noalloc_scratch); });
+  if (s.err != cudaSuccess) return cuda_fail(s.err, "cudaGetSymbolAddress(g_noalloc_scratch)");
+  *out = s.ptr;
+  return B200FA_OK;
+}
+
+}  // namespace
+
+extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq,
+                                  int64_t Hkv, int64_t Nq, int64_t Nk, int64_t D, float scale, int32_t variant,
+                                  int64_t unit_begin, int64_t unit_end, void* stream, const b200fa_options* opts,
+                                  void** scratch_out) {
+  g_last_error[0] = '\0';
+  if (!q || !k || !v || !o) return fail(B200FA_ERR_NULL, "q, k, v and o must be device pointers");
+  int rc = validate_shape(B, Hq, Hkv, Nq, Nk, D);
+  if (rc != B200FA_OK) return rc;
+  if (variant != B200FA_VARIANT_FP16 && variant != B200FA_VARIANT_FP32)
+    return fail(B200FA_ERR_VARIANT, "unknown variant %d", variant);
+  if (!std::isfinite(scale) || !(scale > 0.f)) return fail(B200FA_ERR_SCALE, "scale must be finite and positive");
+  const int64_t units = B * Hq * ceil_div<int64_t>(Nq, kBlockM);
+  if (unit_begin < 0 || unit_end > units || unit_begin > unit_end)
+    return fail(B200FA_ERR_UNIT_RANGE, "unit range [%lld, %lld) outside [0, %lld)", (long long)unit_begin,
+                (long long)unit_end, (long long)units);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(B200FA_ERR_ALIGNMENT, "tensor pointers must be 16-byte aligned");
+  b200fa_options o_default{sizeof(b200fa_options), 0u, 0u, 0};
+  if (opts == nullptr) opts = &o_default;
+  if (opts->struct_size != sizeof(b200fa_options)) return fail(B200FA_ERR_OPTIONS, "b200fa_options.struct_size mismatch");
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int sms = 0;
+  if ((rc = device_setup(dev, &sms)) != B200FA_OK) return rc;
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch(dev, &scratch)) != B200FA_OK) return rc;
+  if (scratch_out) *scratch_out = scratch;
+
+  const int64_t nqb = ceil_div<int64_t>(Nq, kBlockM);
+  const int64_t items = plan_count<int64_t>(nqb, unit_begin, unit_end);
+  if (items == 0) return B200FA_OK;
+  int grid = sms;
+  if (opts->max_ctas > 0 && opts->max_ctas < grid) grid = opts->max_ctas;
+  if (grid > B200FA_MAX_CTAS) grid = B200FA_MAX_CTAS;
+  if (items < grid) grid = int(items);
+  const uint64_t need = uint64_t(B200FA_WS_HEADER_BYTES) +
+                        ((opts->flags & B200FA_FLAG_TRACE) ? uint64_t(B200FA_WS_TRACE_BYTES) * uint64_t(grid) : 0u);
+  if (need > B200FA_NOALLOC_SCRATCH_BYTES)
+    return fail(B200FA_ERR_WORKSPACE,
+                "b200fa_fwd_noalloc: this call needs %llu bytes of scratch (trace records for %d CTAs) but the "
+                "static scratch holds %u (trace for at most %u CTAs); set max_ctas <= %u or drop B200FA_FLAG_TRACE",
+                (unsigned long long)need, grid, (unsigned)B200FA_NOALLOC_SCRATCH_BYTES,
+                (unsigned)B200FA_NOALLOC_TRACE_CTAS, (unsigned)B200FA_NOALLOC_TRACE_CTAS);
+
+  FwdParams p;
+  std::memset(&p, 0, sizeof(p));
+  if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq)) != B200FA_OK) return rc;
+  p.Hq = int32_t(Hq);
+  p.Hkv = int32_t(Hkv);
+  p.group = int32_t(Hq / Hkv);
+  p.nqb = int32_t(nqb);
+  p.n_kv = int32_t(ceil_div<int64_t>(Nk, kBlockN));
+  p.nk_tail = int32_t(Nk - int64_t(p.n_kv - 1) * kBlockN);
+  p.unit_begin = int32_t(unit_begin);
+  p.unit_end = int32_t(unit_end);
+  p.num_items = int32_t(items);
+  p.scale_log2 = float(double(scale) * 1.4426950408889634074);
+  p.flags = opts->flags;
+  p.timeout_ns = uint64_t(opts->timeout_us ? opts->timeout_us : 2000000u) * 1000ull;
+  p.ws = static_cast<uint32_t*>(scratch);
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents: the status header must start
+  // at zero for this call.  Trace records are rewritten by every CTA that runs.
+  e = cudaMemsetAsync(scratch, 0, B200FA_WS_HEADER_BYTES, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(noalloc status header)");
+  if (variant == B200FA_VARIANT_FP16)
+    b200_fa_fp16_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
+  else
+    b200_fa_fp32_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch (noalloc)");
+  return B200FA_OK;
+}

@@ -160,6 +160,40 @@ const char* b200fa_last_error_string(void);
 /* Library version string. */
 const char* b200fa_version(void);
 
+/* Allocation-free forward.  This entry point has no counterpart in the
+ * reference; it exists for callers that cannot hand the library a
+ * workspace: a C or FFI host with no device allocator of its own, a runtime
+ * that has reserved the whole device pool for itself and forbids side
+ * allocations, or a latency-critical path that must not call cudaMalloc
+ * (which can synchronize the device).  Same computation and arguments as
+ * b200fa_fwd_ex minus the workspace: the status header and trace records
+ * live in a static device array of B200FA_NOALLOC_SCRATCH_BYTES bytes
+ * (256-byte header + trace records for at most B200FA_NOALLOC_TRACE_CTAS
+ * CTAs), one copy on every device that loads the library, held until the
+ * process exits.  Nothing is allocated: no cudaMalloc, cudaFree or
+ * allocating library routine is called.
+ *   - The first call on a device resolves that device's copy of the array
+ *     (cudaGetSymbolAddress) and sets the kernel attributes; make that first
+ *     call before any stream capture.
+ *   - Each call clears the status header on `stream` before its launch.
+ *     All calls share the array: calls that overlap on the GPU (e.g. on
+ *     different streams) race on the status header and trace records.
+ *   - A call whose scratch need exceeds the array -- tracing
+ *     (B200FA_FLAG_TRACE) with a persistent grid of more than
+ *     B200FA_NOALLOC_TRACE_CTAS CTAs -- is rejected with
+ *     B200FA_ERR_WORKSPACE before anything is launched; cap the grid with
+ *     opts->max_ctas or trace less.
+ *   - scratch_out (may be NULL) receives the device address of this
+ *     device's scratch, for b200fa_read_status / b200fa_reset_status. */
+#define B200FA_NOALLOC_TRACE_CTAS 128u
+#define B200FA_NOALLOC_SCRATCH_BYTES \
+    (B200FA_WS_HEADER_BYTES + B200FA_WS_TRACE_BYTES * B200FA_NOALLOC_TRACE_CTAS)
+int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, void* o,
+                       int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, int64_t Nk,
+                       int64_t D, float scale, int32_t variant,
+                       int64_t unit_begin, int64_t unit_end,
+                       void* stream, const b200fa_options* opts, void** scratch_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,105 @@
+"""The allocation-free entry point, b200fa_fwd_noalloc, through the C ABI.
+
+Some callers cannot give the library a workspace: a C or FFI host with no
+device allocator of its own, a runtime that has reserved the whole device
+pool and forbids side allocations, or a latency-critical path that must not
+call cudaMalloc because it can synchronize the device.  For them the
+library keeps the kernel's scratch (status header and trace records) in a
+static device array and allocates nothing.
+
+This test calls that entry point twice in a row for each variant and checks
+each output against the workspace-based entry point (b200fa_fwd_ex) within
+the parity bar the other GPU tests use (max-abs <= 2e-3, mean-abs <= 2e-4),
+reads the device status through the returned scratch address, and checks
+that a call whose scratch need exceeds the static array is rejected before
+anything is launched.  The file is named to be collected last, so a run
+that stops at the first failure has run every other test already.
+"""
+
+import ctypes as C
+
+import pytest
+import torch
+
+MAX_ABS = 2e-3
+MEAN_ABS = 2e-4
+
+
+def _inputs(dev):
+    g = torch.Generator().manual_seed(21)
+    q = torch.randn((1, 4, 1000, 128), generator=g).half().to(dev)
+    k = torch.randn((1, 2, 777, 128), generator=g).half().to(dev)
+    v = torch.randn((1, 2, 777, 128), generator=g).half().to(dev)
+    return q, k, v
+
+
+def _call_noalloc(so, q, k, v, out, variant, stream, opts=None):
+    from fa_b200 import lib
+
+    B, Hq, Nq, D = q.shape
+    Hkv, Nk = k.shape[1], k.shape[2]
+    scratch = C.c_void_p()
+    rc = so.b200fa_fwd_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), B, Hq, Hkv, Nq, Nk, D,
+                               D ** -0.5, variant, 0, lib.num_units(B, Hq, Nq), stream,
+                               C.byref(opts) if opts is not None else None, C.byref(scratch))
+    return rc, scratch.value
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("variant", [0, 1], ids=["fp16", "fp32"])
+def test_noalloc_matches_workspace_entry_point_on_two_calls(variant):
+    from fa_b200 import lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    so = lib.load()
+    q, k, v = _inputs(dev)
+    B, Hq, Nq, D = q.shape
+    Hkv, Nk = k.shape[1], k.shape[2]
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    ws = torch.zeros(lib.workspace_size(B, Hq, Hkv, Nq, Nk, D, variant), dtype=torch.uint8, device=dev)
+    ref = torch.empty_like(q)
+    lib.fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), ref.data_ptr(), B, Hq, Hkv, Nq, Nk, D, D ** -0.5, variant,
+            0, lib.num_units(B, Hq, Nq), ws.data_ptr(), ws.numel(), stream)
+    torch.cuda.synchronize(dev)
+
+    for _ in range(2):
+        out = torch.full_like(q, float("nan"))
+        rc, scratch = _call_noalloc(so, q, k, v, out, variant, stream)
+        assert rc == 0, lib.last_error()
+        assert scratch is not None
+        assert lib.read_status(scratch, stream)[0] == lib.DEV_OK
+        d = (out.float() - ref.float()).abs()
+        assert torch.isfinite(out).all()
+        assert float(d.max()) <= MAX_ABS and float(d.mean()) <= MEAN_ABS
+
+
+@pytest.mark.gpu
+def test_noalloc_rejects_scratch_need_beyond_the_static_array():
+    from fa_b200 import lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    so = lib.load()
+    g = torch.Generator().manual_seed(22)
+    q = torch.randn((1, 16, 4096, 128), generator=g).half().to(dev)   # 512 units -> 256 items
+    k = torch.randn((1, 1, 256, 128), generator=g).half().to(dev)
+    v = torch.randn((1, 1, 256, 128), generator=g).half().to(dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    limit = 128  # B200FA_NOALLOC_TRACE_CTAS
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    items = lib.num_units(1, 16, 4096) // 2
+    out = torch.zeros_like(q)
+    if min(sms, items) > limit:  # a traced grid would need more trace records than the array holds
+        opts = lib.Options(C.sizeof(lib.Options), lib.FLAG_TRACE, 0, 0)
+        rc, _ = _call_noalloc(so, q, k, v, out, 1, stream, opts)
+        assert rc == -8, rc  # B200FA_ERR_WORKSPACE
+        assert "static scratch" in lib.last_error()
+        torch.cuda.synchronize(dev)
+        assert torch.count_nonzero(out) == 0  # nothing was launched
+    opts = lib.Options(C.sizeof(lib.Options), lib.FLAG_TRACE, 0, 64)  # 64-CTA grid fits
+    rc, scratch = _call_noalloc(so, q, k, v, out, 1, stream, opts)
+    assert rc == 0, lib.last_error()
+    assert lib.read_status(scratch, stream)[0] == lib.DEV_OK
+    assert torch.isfinite(out).all()
