@@ -22,6 +22,9 @@
 
 using namespace b200fa;
 
+static_assert(kTimelineOffset == B200FA_WS_TIMELINE_OFFSET, "timeline offset mismatch");
+static_assert(kTimelineBlocks == int(B200FA_TIMELINE_BLOCKS), "timeline size mismatch");
+
 __global__ void __launch_bounds__(kThreads, 1) b200_fa_fp16_kernel(const __grid_constant__ FwdParams p) {
   attention_fwd_body<0>(p);
 }
@@ -141,7 +144,7 @@ int64_t b200fa_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, in
   if (rc != B200FA_OK) return rc;
   if (variant != B200FA_VARIANT_FP16 && variant != B200FA_VARIANT_FP32)
     return fail(B200FA_ERR_VARIANT, "unknown variant %d", variant);
-  return int64_t(B200FA_WS_HEADER_BYTES) + int64_t(B200FA_WS_TRACE_BYTES) * B200FA_MAX_CTAS;
+  return int64_t(B200FA_WS_TIMELINE_OFFSET) + int64_t(B200FA_WS_TIMELINE_BYTES);
 }
 
 int64_t b200fa_plan_item(int64_t B, int64_t Hq, int64_t Nq, int64_t unit_begin, int64_t unit_end, int64_t index,
@@ -173,7 +176,7 @@ int b200fa_fwd_ex(const void* q, const void* k, const void* v, void* o, int64_t 
                 (long long)unit_end, (long long)units);
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
     return fail(B200FA_ERR_ALIGNMENT, "tensor pointers must be 16-byte aligned");
-  const uint64_t ws_need = uint64_t(B200FA_WS_HEADER_BYTES) + uint64_t(B200FA_WS_TRACE_BYTES) * B200FA_MAX_CTAS;
+  const uint64_t ws_need = uint64_t(B200FA_WS_TIMELINE_OFFSET) + uint64_t(B200FA_WS_TIMELINE_BYTES);
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 || ws_bytes < ws_need)
     return fail(B200FA_ERR_WORKSPACE, "workspace must be 256-byte aligned and at least %llu bytes",
                 (unsigned long long)ws_need);
@@ -330,8 +333,10 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
   if (opts->max_ctas > 0 && opts->max_ctas < grid) grid = opts->max_ctas;
   if (grid > B200FA_MAX_CTAS) grid = B200FA_MAX_CTAS;
   if (items < grid) grid = int(items);
-  const uint64_t need = uint64_t(B200FA_WS_HEADER_BYTES) +
-                        ((opts->flags & B200FA_FLAG_TRACE) ? uint64_t(B200FA_WS_TRACE_BYTES) * uint64_t(grid) : 0u);
+  const uint64_t need = (opts->flags & B200FA_FLAG_TIMELINE)
+                            ? uint64_t(B200FA_WS_TIMELINE_OFFSET) + B200FA_WS_TIMELINE_BYTES
+                            : uint64_t(B200FA_WS_HEADER_BYTES) +
+                                  ((opts->flags & B200FA_FLAG_TRACE) ? uint64_t(B200FA_WS_TRACE_BYTES) * uint64_t(grid) : 0u);
   if (need > B200FA_NOALLOC_SCRATCH_BYTES)
     return fail(B200FA_ERR_WORKSPACE,
                 "b200fa_fwd_noalloc: this call needs %llu bytes of scratch (trace records for %d CTAs) but the "

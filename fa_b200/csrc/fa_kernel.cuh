@@ -12,11 +12,12 @@
 // tile repeats the first one's rows and is not stored.  Items are dealt
 // round-robin to a persistent grid of one CTA per SM.
 //
-// CTA roles (320 threads):
+// CTA roles (384 threads = 3 warpgroups):
 //   warps 0-3   softmax warpgroup 0: query tile 0 (TMEM lanes = rows)
 //   warps 4-7   softmax warpgroup 1: query tile 1
 //   warp  8     MMA issuer (one thread): tcgen05.mma for QK^T and PV
 //   warp  9     TMA producer (one thread): Q tiles and the K/V ring
+//   warps 10-11 idle (complete warpgroup 2 for the register split)
 //
 // Tensor memory (512 columns x 128 lanes x 32 bit):
 //   [  0,128) S0 = Q0 K^T (FP32); its first 64 columns are reused for P0
@@ -60,27 +61,35 @@ constexpr int kHeadDim = 128;   // head dimension (fixed)
 constexpr int kStages = 4;      // K/V ring depth
 constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 32 KiB
 constexpr int kHalfTileBytes = kTileBytes / 2;      // one TMA box: 64 cols x 128 rows
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;    // 3 warpgroups
 constexpr int kMmaWarp = 8;
-constexpr int kLoadWarp = 9;
+constexpr int kLoadWarp = 9;     // warps 10-11 complete warpgroup 2 and idle
+// Register split (setmaxnreg): launch 384 x 168 = 64512; softmax warpgroups
+// 256 x 208 + warpgroup 2 128 x 88 = 64512.
+constexpr uint32_t kLaunchRegs = 168;
+constexpr uint32_t kSoftmaxRegs = 208;
+constexpr uint32_t kControlRegs = 88;
+static_assert(256 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs, "register split exceeds the launch budget");
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (factor 256)
 
 // Barrier slots.
-constexpr int kBarQFull = 0;     // [2] Q tile landed            (tx bytes)
-constexpr int kBarQEmpty = 2;    // [2] Q buffer free            (epilogue)
-constexpr int kBarSFull = 4;     // [2] S tile computed          (tcgen05.commit)
-constexpr int kBarPFull = 6;     // [2] P written, O corrected   (128 threads)
-constexpr int kBarOFinal = 8;    // [2] last PV of the item done (tcgen05.commit)
-constexpr int kBarOStaged = 10;  // [2] O tile staged in smem    (128 threads)
-constexpr int kBarDrain = 12;    // MMA drain at exit            (tcgen05.commit)
-constexpr int kBarKVFull = 13;   // [kStages]
+constexpr int kBarQFull = 0;     // [2] Q tile landed                     (tx bytes)
+constexpr int kBarQEmpty = 2;    // [2] Q buffer free                     (epilogue store issued)
+constexpr int kBarSFull = 4;     // [2] S tile computed                   (tcgen05.commit)
+constexpr int kBarPFull = 6;     // [2] P of keys 64-127 written          (128 threads)
+constexpr int kBarOFinal = 8;    // [2] last PV of the item done          (tcgen05.commit)
+constexpr int kBarOStaged = 10;  // [2] O tile staged in smem             (128 threads)
+constexpr int kBarDrain = 12;    // MMA drain at exit                     (tcgen05.commit)
+constexpr int kBarPHalf = 13;    // [2] P of keys 0-63 written, O corrected (128 threads)
+constexpr int kBarTurn = 15;     // [2] softmax turn token of warpgroup t (128 threads)
+constexpr int kBarKVFull = 17;   // [kStages]
 constexpr int kBarKVEmpty = kBarKVFull + kStages;  // [kStages]
 constexpr int kNumBars = kBarKVEmpty + kStages;
 
 constexpr int kSmemQ = 0;
 constexpr int kSmemKV = 2 * kTileBytes;
 constexpr int kSmemBar = kSmemKV + kStages * kTileBytes;
-constexpr int kSmemMisc = kSmemBar + kNumBars * 8;
+constexpr int kSmemMisc = kSmemBar + kNumBars * 8;  // TMEM base (4 B), abort flag (4 B)
 constexpr int kSmemUsed = kSmemMisc + 16;
 constexpr int kSmemBytes = kSmemUsed + 1024;  // + slack for 1024-B alignment
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
@@ -95,19 +104,56 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdescQK = (1u << 4) | (uint32_t(kBlockN >> 3) << 17) | (uint32_t(kBlockM >> 4) << 24);
 constexpr uint32_t kIdescPV = (1u << 4) | (1u << 16) | (uint32_t(kHeadDim >> 3) << 17) | (uint32_t(kBlockM >> 4) << 24);
 
-// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version bit.
-// K-major operand (Q, K): rows of 128 B, 8-row groups 1024 B apart (SBO);
-// the leading offset is unused for swizzled K-major layouts.
-__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
-  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
-         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+// Shared-memory matrix descriptors (PTX ISA "Matrix Descriptor"), 128-byte
+// swizzle, sm_100 version bit.  Low word: start address >> 4 (bits 0-13),
+// leading byte offset >> 4 (bits 16-29).  High word: stride byte offset >> 4
+// (bits 0-13), version 1 (bit 14), layout SWIZZLE_128B = 2 (bits 29-31).
+//  * K-major operand (Q, K): rows of 128 B, 8-row groups 1024 B apart (SBO);
+//    the leading offset is unused for swizzled K-major layouts (set to 16 B).
+//  * MN-major operand (V as the B matrix of P*V, head dim contiguous):
+//    64-element column blocks kHalfTileBytes apart (LBO), 8-key groups
+//    1024 B apart (SBO).
+constexpr uint32_t kDescHi = uint32_t(1024 >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t desc_lo_kmajor(uint32_t saddr) { return ((saddr & 0x3FFFFu) >> 4) | (1u << 16); }
+__device__ __forceinline__ uint32_t desc_lo_mnmajor(uint32_t saddr) {
+  return ((saddr & 0x3FFFFu) >> 4) | (uint32_t(kHalfTileBytes >> 4) << 16);
 }
-// MN-major operand (V as the B matrix of P*V: N = head dim contiguous):
-// 64-element column blocks kHalfTileBytes apart (LBO), 8-key groups 1024 B
-// apart (SBO).
-__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr) {
-  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(kHalfTileBytes >> 4) << 16) |
-         (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+
+// exp2 on the FMA pipe for two lanes.  Cody-Waite split x = n + f with
+// n = round(x) taken from the low mantissa bits of x + 1.5*2^23 and
+// f = x - n in [-1/2, 1/2]; 2^f by the degree-3 minimax polynomial of
+// fit_exp2_poly.py (relative error 7.5e-5, below FP16's half-ulp); n added to
+// the exponent field as an integer.  x is clamped at -120 first so the
+// exponent cannot wrap; 2^-120 is 0 in FP16 and negligible in the FP32 row
+// sum, and masked keys (x = -inf) land there too.
+constexpr int kPolyPairs = 2;  // of every 8 key pairs, these go to the polynomial
+// The two softmax warpgroups share all four SMSPs; with kPingPong they take
+// strict turns (tile 0, tile 1, tile 0, ...) so each runs at the full issue
+// and MUFU rate while the tensor pipe works on the other tile.
+constexpr bool kPingPong = false;
+constexpr float kExp2C0 = 0.9999280571937561f;
+constexpr float kExp2C1 = 0.6932609677314758f;
+constexpr float kExp2C2 = 0.2426111251115799f;
+constexpr float kExp2C3 = 0.0551716685295105f;
+
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  float a, b;
+  f2_unpack(x2, a, b);
+  const uint64_t xc = f2_pack(fmaxf(a, -120.f), fmaxf(b, -120.f));
+  const uint64_t r = f2_add(xc, f2_pack(12582912.f, 12582912.f));     // round to integer
+  const uint64_t nf = f2_add(r, f2_pack(-12582912.f, -12582912.f));   // n as a float
+  const uint64_t f = f2_fma(nf, f2_pack(-1.f, -1.f), xc);             // x - n
+  uint64_t q = f2_fma(f2_pack(kExp2C3, kExp2C3), f, f2_pack(kExp2C2, kExp2C2));
+  q = f2_fma(q, f, f2_pack(kExp2C1, kExp2C1));
+  q = f2_fma(q, f, f2_pack(kExp2C0, kExp2C0));
+  float qa, qb, ra, rb;
+  f2_unpack(q, qa, qb);
+  f2_unpack(r, ra, rb);
+  // r's bits are 0x4B400000 + n; times 2^23 only n << 23 survives (one mad).
+  uint32_t ea, eb;
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(ea) : "r"(__float_as_uint(ra)), "r"(__float_as_uint(qa)));
+  asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(eb) : "r"(__float_as_uint(rb)), "r"(__float_as_uint(qb)));
+  return f2_pack(__uint_as_float(ea), __uint_as_float(eb));
 }
 
 struct FwdParams {
@@ -129,6 +175,26 @@ struct FwdParams {
 
 constexpr uint32_t kFlagTrace = 1u;
 constexpr uint32_t kFlagTestWithholdP = 2u;
+constexpr uint32_t kFlagTimeline = 4u;
+
+// Debug timeline (kFlagTimeline): CTA 0 stamps clock64() at fixed points of
+// its first work item's first kTimelineBlocks key blocks.  Layout: u64
+// [role][block][event] at byte kTimelineOffset of the workspace; roles
+// 0/1 = softmax tile 0/1 (warp 4t, lane 0), 2 = MMA thread, 3 = TMA thread.
+constexpr int kTimelineBlocks = 48;
+constexpr uint32_t kTimelineOffset = 256u + 32u * 1024u;
+
+struct Timeline {
+  uint64_t* base;  // nullptr when not recording
+  __device__ __forceinline__ void mark(int role, int j, int e) const {
+    if (base != nullptr && j < kTimelineBlocks) base[(role * kTimelineBlocks + j) * 8 + e] = clock64();
+  }
+};
+
+__device__ __forceinline__ Timeline make_timeline(const FwdParams& p, int it) {
+  const bool on = (p.flags & kFlagTimeline) != 0 && blockIdx.x == 0 && it == 0;
+  return Timeline{on ? reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p.ws) + kTimelineOffset) : nullptr};
+}
 
 template <typename I>
 __host__ __device__ __forceinline__ I ceil_div(I a, I b) {
@@ -225,25 +291,22 @@ struct Smem {
   __device__ __forceinline__ uint32_t kv(uint32_t s) const { return base + kSmemKV + s * kTileBytes; }
   __device__ __forceinline__ uint32_t tmem_slot() const { return base + kSmemMisc; }
   __device__ __forceinline__ uint32_t abort_slot() const { return base + kSmemMisc + 4; }
+
 };
 
 // ------------------------------------------------------------------ roles
+// S = Q K^T over the full head dim (8 K-major steps, overwrite).
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_smem, uint32_t k_smem) {
-#pragma unroll
-  for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * kHalfTileBytes + (kk & 3) * 32;
-    mma_ss(d_tmem, desc_kmajor(q_smem + off), desc_kmajor(k_smem + off), kIdescQK, kk > 0 ? 1u : 0u);
-  }
+  mma_ss_k128(d_tmem, desc_lo_kmajor(q_smem), desc_lo_kmajor(k_smem), kDescHi, kIdescQK, 0u);
 }
 
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem,
-                                         bool accumulate) {
-#pragma unroll
-  for (int kk = 0; kk < kBlockN / 16; ++kk) {
-    // A = P columns [8kk, 8kk+8) (16 FP16 keys); B = V rows [16kk, 16kk+16).
-    mma_ts(d_tmem, p_tmem + kk * 8, desc_mnmajor(v_smem + kk * 2048), kIdescPV,
-           (accumulate || kk > 0) ? 1u : 0u);
-  }
+// O (+)= P V over keys [64*half, 64*half + 64): A = P's TMEM columns
+// [64*half, 64*half + 32) (FP16 pairs; each key half's P sits at the start of
+// that half's own S columns), B = V rows of those keys.
+template <int half>
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem, bool accumulate) {
+  mma_ts_k64(d_tmem, p_tmem + 64 * half, desc_lo_mnmajor(v_smem) + 512 * half, kDescHi, kIdescPV,
+             (half > 0 || accumulate) ? 1u : 0u);
 }
 
 __device__ void mma_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base, const Waiter& w) {
@@ -255,6 +318,7 @@ __device__ void mma_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base,
   uint32_t p_phase = 0;  // bit t: phase of P-full[t]
   bool ok = true;
   for (int item = blockIdx.x, it = 0; ok && item < p.num_items; item += gridDim.x, ++it) {
+    const Timeline tl = make_timeline(p, it);
     const uint32_t ip = uint32_t(it) & 1u;
     uint32_t sk = kv_it % kStages;
     if (!w.wait(sm.bar(kBarQFull + 0), ip, site | (kBarQFull + 0))) break;
@@ -269,14 +333,21 @@ __device__ void mma_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base,
     mma_commit(sm.bar(kBarKVEmpty + sk));
     ++kv_it;
     for (int j = 0; j < n; ++j) {
+      tl.mark(2, j, 0);
       const uint32_t sv = kv_it % kStages;
       const uint32_t vph = (kv_it / kStages) & 1u;
       ++kv_it;
       if (!w.wait(sm.bar(kBarKVFull + sv), vph, site | (kBarKVFull + sv))) { ok = false; break; }
+      tl.mark(2, j, 1);
+      if (!w.wait(sm.bar(kBarPHalf + 0), p_phase & 1u, site | (kBarPHalf + 0))) { ok = false; break; }
+      tl.mark(2, j, 2);
+      tc_fence_after();
+      issue_pv<0>(tO0, tS0, sm.kv(sv), j > 0);
       if (!w.wait(sm.bar(kBarPFull + 0), p_phase & 1u, site | (kBarPFull + 0))) { ok = false; break; }
+      tl.mark(2, j, 3);
       p_phase ^= 1u;
       tc_fence_after();
-      issue_pv(tO0, tS0, sm.kv(sv), j > 0);
+      issue_pv<1>(tO0, tS0, sm.kv(sv), true);
       if (j == n - 1) mma_commit(sm.bar(kBarOFinal + 0));
       const bool more = j + 1 < n;
       uint32_t sk2 = 0;
@@ -286,20 +357,27 @@ __device__ void mma_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base,
           ok = false;
           break;
         }
+        tl.mark(2, j, 4);
         tc_fence_after();
         issue_qk(tS0, sm.q(0), sm.kv(sk2));
         mma_commit(sm.bar(kBarSFull + 0));
       }
+      if (!w.wait(sm.bar(kBarPHalf + 1), (p_phase >> 1) & 1u, site | (kBarPHalf + 1))) { ok = false; break; }
+      tl.mark(2, j, 5);
+      tc_fence_after();
+      issue_pv<0>(tO1, tS1, sm.kv(sv), j > 0);
       if (!w.wait(sm.bar(kBarPFull + 1), (p_phase >> 1) & 1u, site | (kBarPFull + 1))) { ok = false; break; }
+      tl.mark(2, j, 6);
       p_phase ^= 2u;
       tc_fence_after();
-      issue_pv(tO1, tS1, sm.kv(sv), j > 0);
+      issue_pv<1>(tO1, tS1, sm.kv(sv), true);
       mma_commit(sm.bar(kBarKVEmpty + sv));
       if (j == n - 1) mma_commit(sm.bar(kBarOFinal + 1));
       if (more) {
         issue_qk(tS1, sm.q(1), sm.kv(sk2));
         mma_commit(sm.bar(kBarSFull + 1));
         mma_commit(sm.bar(kBarKVEmpty + sk2));
+        tl.mark(2, j, 7);
         ++kv_it;
       }
     }
@@ -325,6 +403,7 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w) {
     const int row0 = qb * kBlockM;
     const int row1 = cnt == 2 ? row0 + kBlockM : row0;
     const uint32_t ip = uint32_t(it) & 1u;
+    const Timeline tl = make_timeline(p, it);
     if (!w.wait(sm.bar(kBarQEmpty + 0), ip ^ 1u, site | (kBarQEmpty + 0))) break;
     mbar_arrive_expect_tx(sm.bar(kBarQFull + 0), kTileBytes);
     tma_load_3d(sm.q(0), &p.tm_q, sm.bar(kBarQFull + 0), 0, row0, bh);
@@ -337,7 +416,9 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w) {
         const uint32_t s = kv_it % kStages;
         const uint32_t ph = (kv_it / kStages) & 1u;
         ++kv_it;
+        tl.mark(3, j, 2 * which);
         if (!w.wait(sm.bar(kBarKVEmpty + s), ph ^ 1u, site | (kBarKVEmpty + s))) { ok = false; break; }
+        tl.mark(3, j, 2 * which + 1);
         const CUtensorMap* map = which == 0 ? &p.tm_k : &p.tm_v;
         mbar_arrive_expect_tx(sm.bar(kBarKVFull + s), kTileBytes);
         tma_load_3d(sm.kv(s), map, sm.bar(kBarKVFull + s), 0, j * kBlockN, kvh);
@@ -366,6 +447,77 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w) {
   }
 }
 
+// Exponentials of 64 keys (32 pairs) of one row: x = s * scale*log2(e) - m
+// with packed FP32 FMAs; of every 8 pairs the last kPoly go through the
+// FMA-pipe polynomial (exp2_poly2) and the rest through MUFU (FP32 ex2, or
+// FP16x2 ex2 in the FP16 variant).  Writes 32 packed FP16 pairs of P and adds
+// to the running row-sum accumulators.
+template <int kVariant, int kPoly>
+__device__ __forceinline__ void exp_keys64(const uint32_t* r, uint64_t sl2x2, uint64_t nmx2, uint32_t* pk,
+                                           uint64_t& acc0, uint64_t& acc1, float& hsum) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    uint32_t hacc = 0u;
+#pragma unroll
+    for (int pp = 0; pp < 8; ++pp) {
+      const int i = g * 8 + pp;  // key pair index within the 64 keys
+      const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sl2x2, nmx2);
+      if (pp >= 8 - kPoly) {
+        const uint64_t p2 = exp2_poly2(x2);
+        if (pp & 1) acc1 = f2_add(acc1, p2); else acc0 = f2_add(acc0, p2);
+        float a, b;
+        f2_unpack(p2, a, b);
+        pk[i] = pack_h2(a, b);
+      } else if constexpr (kVariant == 1) {
+        float a, b;
+        f2_unpack(x2, a, b);
+        const float ea = ex2_approx(a), eb = ex2_approx(b);
+        const uint64_t p2 = f2_pack(ea, eb);
+        if (pp & 1) acc1 = f2_add(acc1, p2); else acc0 = f2_add(acc0, p2);
+        pk[i] = pack_h2(ea, eb);
+      } else {
+        float a, b;
+        f2_unpack(x2, a, b);
+        const uint32_t e2 = ex2_approx_h2(pack_h2(a, b));
+        pk[i] = e2;
+        hacc = (pp == 0) ? e2 : hadd2(hacc, e2);
+      }
+    }
+    if constexpr (kVariant == 0) {
+      if (kPoly < 8) hsum += h2_sum_f32(hacc);
+    }
+  }
+}
+
+// Keys at or beyond `valid` (the last block's key count) get score -inf.
+__device__ __forceinline__ void mask_keys(uint32_t* r, int first_key, int valid) {
+#pragma unroll
+  for (int i = 0; i < 64; ++i)
+    if (first_key + i >= valid) r[i] = __float_as_uint(-INFINITY);
+}
+
+// Row maximum of 64 scores: 3-input max, four independent chains.
+__device__ __forceinline__ float row_max64(const uint32_t* r) {
+  float mc0 = -INFINITY, mc1 = -INFINITY, mc2 = -INFINITY, mc3 = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 64; i += 8) {
+    mc0 = max3(mc0, __uint_as_float(r[i + 0]), __uint_as_float(r[i + 1]));
+    mc1 = max3(mc1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+    mc2 = max3(mc2, __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+    mc3 = max3(mc3, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+  }
+  return fmaxf(fmaxf(mc0, mc1), fmaxf(mc2, mc3));
+}
+
+// Softmax of one query tile per warpgroup (warps 0-3: tile 0, 4-7: tile 1),
+// one thread per query row (its TMEM lane), all 128 keys of a block.
+//
+// After a tile's first block the exponentials of keys 0-63 are computed
+// speculatively against the current reference maximum while the block's row
+// maximum is reduced; they are redone only if that maximum exceeds the
+// reference by more than 2^kRescaleLog2 (rare once it has settled).  P goes to
+// the MMA warp in two halves: keys 0-63 into TMEM columns 0-31 of the tile's
+// S region, keys 64-127 into columns 64-95.
 template <int kVariant>  // 0 = FP16 softmax, 1 = FP32 softmax
 __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base, const Waiter& w,
                              uint32_t warp, uint32_t lane) {
@@ -378,39 +530,50 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
   const uint32_t sQ = sm.q(t);
   const uint32_t site = warp << 8;
   const float sl2 = p.scale_log2;
+  const uint64_t sl2x2 = f2_pack(sl2, sl2);
   const int n = p.n_kv;
   const bool withhold = (p.flags & kFlagTestWithholdP) != 0 && t == 1;
   uint32_t s_phase = 0;
+  uint32_t turns = 0;  // ping-pong turns taken
   bool ok = true;
 
   for (int item = blockIdx.x, it = 0; ok && item < p.num_items; item += gridDim.x, ++it) {
     float m_ref = -INFINITY;  // reference maximum, log2 domain
     float l = 0.f;
+    const Timeline tl = (wq == 0 && lane == 0) ? make_timeline(p, it) : Timeline{nullptr};
     for (int j = 0; j < n; ++j) {
       if (!w.wait(sm.bar(kBarSFull + t), s_phase, site | (kBarSFull + t))) { ok = false; break; }
+      tl.mark(t, j, 0);
       s_phase ^= 1u;
+      if (kPingPong) {  // warpgroup 0's first turn is free (parity trick)
+        if (!w.wait(sm.bar(kBarTurn + t), (turns & 1u) ^ (t == 0 ? 1u : 0u), site | (kBarTurn + t))) { ok = false; break; }
+        ++turns;
+      }
       tc_fence_after();
-      uint32_t r[128];
-      tmem_ld32(tS + 0, r + 0);
-      tmem_ld32(tS + 32, r + 32);
-      tmem_ld32(tS + 64, r + 64);
-      tmem_ld32(tS + 96, r + 96);
+      // Keys 0-63: load, exponentiate speculatively against the current
+      // reference (after the first block), and reduce their maximum.
+      const bool tail = (j == n - 1 && p.nk_tail < kBlockN);
+      uint32_t pk[64];
+      uint64_t acc0 = 0ull, acc1 = 0ull;  // packed FP32 partial row sums
+      float hsum = 0.f;                   // FP16 variant: sums of FP16 group sums
+      float mx;
+      {
+        uint32_t r[64];
+        tmem_ld32(tS + 0, r + 0);
+        tmem_ld32(tS + 32, r + 32);
+        tmem_wait_ld();
+        tl.mark(t, j, 1);
+        if (tail) mask_keys(r, 0, p.nk_tail);
+        if (j > 0) exp_keys64<kVariant, kPolyPairs>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
+        mx = row_max64(r);
+      }
+      // Keys 64-127: load and reduce (their exponentials follow the check).
+      uint32_t r1[64];
+      tmem_ld32(tS + 64, r1 + 0);
+      tmem_ld32(tS + 96, r1 + 32);
       tmem_wait_ld();
-      if (j == n - 1 && p.nk_tail < kBlockN) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i >= p.nk_tail) r[i] = __float_as_uint(-INFINITY);
-      }
-      float mx0 = __uint_as_float(r[0]), mx1 = __uint_as_float(r[1]);
-      float mx2 = __uint_as_float(r[2]), mx3 = __uint_as_float(r[3]);
-#pragma unroll
-      for (int i = 4; i < 128; i += 4) {
-        mx0 = fmaxf(mx0, __uint_as_float(r[i + 0]));
-        mx1 = fmaxf(mx1, __uint_as_float(r[i + 1]));
-        mx2 = fmaxf(mx2, __uint_as_float(r[i + 2]));
-        mx3 = fmaxf(mx3, __uint_as_float(r[i + 3]));
-      }
-      const float m_blk = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+      if (tail) mask_keys(r1, 64, p.nk_tail);
+      const float m_blk = fmaxf(mx, row_max64(r1)) * sl2;
       float alpha = 1.f;
       bool moved = false;
       if (m_blk > m_ref + kRescaleLog2) {
@@ -419,47 +582,11 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
         moved = true;
       }
       l *= alpha;
-      const float nm = -m_ref;
-      uint32_t pk[64];
-      if constexpr (kVariant == 1) {
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(r[2 * i + 0]), sl2, nm));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), sl2, nm));
-          const float p2 = ex2_approx(fmaf(__uint_as_float(r[2 * i + 2]), sl2, nm));
-          const float p3 = ex2_approx(fmaf(__uint_as_float(r[2 * i + 3]), sl2, nm));
-          a0 += p0;
-          a1 += p1;
-          a2 += p2;
-          a3 += p3;
-          pk[i] = pack_h2(p0, p1);
-          pk[i + 1] = pack_h2(p2, p3);
-        }
-        l += (a0 + a1) + (a2 + a3);
-      } else {
-        // Exponent arguments rounded to FP16, two FP16 exp2 per MUFU op,
-        // row sums over groups of 16 in FP16, then FP32.
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          uint32_t s8[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int e = 2 * (g * 8 + i);
-            const uint32_t x2 = pack_h2(fmaf(__uint_as_float(r[e]), sl2, nm),
-                                        fmaf(__uint_as_float(r[e + 1]), sl2, nm));
-            s8[i] = ex2_approx_h2(x2);
-            pk[g * 8 + i] = s8[i];
-          }
-          const uint32_t q0 = hadd2(hadd2(s8[0], s8[1]), hadd2(s8[2], s8[3]));
-          const uint32_t q1 = hadd2(hadd2(s8[4], s8[5]), hadd2(s8[6], s8[7]));
-          l += h2_sum_f32(hadd2(q0, q1));
-        }
-      }
-      tmem_st32(tS + 0, pk);
-      tmem_st32(tS + 32, pk + 32);
+      tl.mark(t, j, 2);
+      // Lazy correction of the running output before any of this block's P
+      // is handed over.  PV_t(j-1) is complete: the commit that signalled
+      // S_t(j) covers it.  The P stores' wait below also covers these stores.
       if (j > 0 && __any_sync(0xffffffffu, moved)) {
-        // PV_t(j-1) is complete: the commit that signalled S_t(j) covers it.
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -470,9 +597,37 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
           tmem_st32(tO + 32 * c, o);
         }
       }
+      if (__any_sync(0xffffffffu, moved)) {
+        // First block, or the reference moved: recompute keys 0-63 from S,
+        // which is still in TMEM (P has not been written yet).
+        uint32_t r[64];
+        tmem_ld32(tS + 0, r + 0);
+        tmem_ld32(tS + 32, r + 32);
+        tmem_wait_ld();
+        if (tail) mask_keys(r, 0, p.nk_tail);
+        if (moved) {
+          acc0 = 0ull;
+          acc1 = 0ull;
+          hsum = 0.f;
+          exp_keys64<kVariant, kPolyPairs>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
+        }
+      }
+      tmem_st32(tS, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(sm.bar(kBarPHalf + t));
+      tl.mark(t, j, 3);
+      exp_keys64<kVariant, kPolyPairs>(r1, sl2x2, f2_pack(-m_ref, -m_ref), pk + 32, acc0, acc1, hsum);
+      tmem_st32(tS + 64, pk + 32);
       tmem_wait_st();
       tc_fence_before();
       if (!(withhold && it == 0 && j == 0)) mbar_arrive(sm.bar(kBarPFull + t));
+      if (kPingPong) mbar_arrive(sm.bar(kBarTurn + (1 - t)));
+      tl.mark(t, j, 4);
+      float a0, b0, a1, b1;
+      f2_unpack(acc0, a0, b0);
+      f2_unpack(acc1, a1, b1);
+      l += ((a0 + b0) + (a1 + b1)) + hsum;
     }
     if (!ok) break;
 
@@ -534,8 +689,10 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
       mbar_init(sm.bar(kBarQEmpty + t), 1);
       mbar_init(sm.bar(kBarSFull + t), 1);
       mbar_init(sm.bar(kBarPFull + t), 128);
+      mbar_init(sm.bar(kBarPHalf + t), 128);
       mbar_init(sm.bar(kBarOFinal + t), 1);
       mbar_init(sm.bar(kBarOStaged + t), 128);
+      mbar_init(sm.bar(kBarTurn + t), 128);
     }
     mbar_init(sm.bar(kBarDrain), 1);
     for (int s = 0; s < kStages; ++s) {
@@ -562,11 +719,15 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
   const Waiter w{sm.abort_slot(), p.timeout_ns, p.ws};
 
   if (warp < 8) {
+    regs_increase<kSoftmaxRegs>();
     softmax_role<kVariant>(p, sm, tmem_base, w, warp, lane);
-  } else if (warp == kMmaWarp) {
-    if (lane == 0) mma_role(p, sm, tmem_base, w);
   } else {
-    if (lane == 0) load_role(p, sm, w);
+    regs_decrease<kControlRegs>();
+    if (warp == kMmaWarp) {
+      if (lane == 0) mma_role(p, sm, tmem_base, w);
+    } else if (warp == kLoadWarp) {
+      if (lane == 0) load_role(p, sm, w);
+    }
   }
   __syncwarp();
   tc_fence_before();

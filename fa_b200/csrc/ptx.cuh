@@ -110,6 +110,16 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Per-warpgroup register budget (all four warps of a warpgroup execute it).
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
@@ -153,6 +163,77 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// One 128x128x128 product as 8 K=16 steps in a single asm block, so the
+// issuing thread spends ~2 integer adds per MMA.  Descriptors are passed as
+// their low words (start-address field in bits 0-13, in 16-byte units) plus
+// the common high word; step kk adds a_step(kk)/b_step(kk) to the low words
+// (the field cannot carry: shared addresses are below 256 KiB).
+//   SS K-major operands (Q, K): step offset (kk/4)*1024 + (kk%4)*2  [16 B]
+//   TS with MN-major B (V):     step offset kk*128                 [16 B],
+//                               A (P in TMEM) advances 8 columns per step.
+// `first_acc` selects accumulate-into-D for step 0; later steps accumulate.
+__device__ __forceinline__ void mma_ss_k128(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
+                                            uint32_t idesc, uint32_t first_acc) {
+  asm volatile(
+      "{\n\t"
+      ".reg .b32 al, bl;\n\t"
+      ".reg .b64 da, db;\n\t"
+      ".reg .pred pf, pt;\n\t"
+      "setp.ne.b32 pf, %5, 0;\n\t"
+      "setp.eq.b32 pt, %4, %4;\n\t"
+      "mov.b64 da, {%1, %3};\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pf;\n\t"
+      "add.u32 al, %1, 2;\n\t add.u32 bl, %2, 2;\n\t"
+      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, 4;\n\t add.u32 bl, %2, 4;\n\t"
+      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, 6;\n\t add.u32 bl, %2, 6;\n\t"
+      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, 1024;\n\t add.u32 bl, %2, 1024;\n\t"
+      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, 1026;\n\t add.u32 bl, %2, 1026;\n\t"
+      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, 1028;\n\t add.u32 bl, %2, 1028;\n\t"
+      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, 1030;\n\t add.u32 bl, %2, 1030;\n\t"
+      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(first_acc)
+      : "memory");
+}
+
+// Four K=16 steps (64 keys) of O += P * V: A from TMEM columns a_tmem + 8*i,
+// B = V rows 16*i.. at b_lo + 128*i.  `first_acc` applies to the first step.
+__device__ __forceinline__ void mma_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
+                                           uint32_t idesc, uint32_t first_acc) {
+  asm volatile(
+      "{\n\t"
+      ".reg .b32 ta, bl;\n\t"
+      ".reg .b64 db;\n\t"
+      ".reg .pred pf, pt;\n\t"
+      "setp.ne.b32 pf, %5, 0;\n\t"
+      "setp.eq.b32 pt, %4, %4;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, pf;\n\t"
+      "add.u32 ta, %1, 8;\n\t add.u32 bl, %2, 128;\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
+      "add.u32 ta, %1, 16;\n\t add.u32 bl, %2, 256;\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
+      "add.u32 ta, %1, 24;\n\t add.u32 bl, %2, 384;\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
+      "}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(first_acc)
       : "memory");
 }
 
@@ -239,6 +320,37 @@ __device__ __forceinline__ float h2_sum_f32(uint32_t a) {
       : "=f"(lo), "=f"(hi)
       : "r"(a));
   return lo + hi;
+}
+
+// ---------------------------------------------------------------- packed FP32
+// Two FP32 lanes in one 64-bit register; one sm_100 f32x2 instruction does
+// the same operation on both (half the issue slots of two scalar ops).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,

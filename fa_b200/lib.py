@@ -22,6 +22,7 @@ VARIANTS = {"fp16": VARIANT_FP16, "fp32": VARIANT_FP32}
 
 FLAG_TRACE = 1
 FLAG_TEST_WITHHOLD_P = 2
+FLAG_TIMELINE = 4
 
 DEV_OK = 0
 DEV_TIMEOUT = 1
@@ -29,6 +30,10 @@ DEV_TIMEOUT = 1
 WS_HEADER_BYTES = 256
 WS_TRACE_BYTES = 32
 MAX_CTAS = 1024
+TIMELINE_BLOCKS = 48
+WS_TIMELINE_OFFSET = WS_HEADER_BYTES + WS_TRACE_BYTES * MAX_CTAS
+WS_TIMELINE_BYTES = 4 * TIMELINE_BLOCKS * 8 * 8
+WS_BYTES = WS_TIMELINE_OFFSET + WS_TIMELINE_BYTES
 
 # name -> (restype, argtypes); the exported C ABI, one entry per declaration
 # of include/b200fa.h.

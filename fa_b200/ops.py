@@ -70,8 +70,7 @@ class Operator:
     def workspace(self, device) -> torch.Tensor:
         ws = self.workspaces.get(device)
         if ws is None:
-            nbytes = lib.WS_HEADER_BYTES + lib.WS_TRACE_BYTES * lib.MAX_CTAS
-            ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+            ws = torch.zeros(lib.WS_BYTES, dtype=torch.uint8, device=device)
             self.workspaces[device] = ws
         return ws
 
@@ -106,11 +105,19 @@ class Operator:
         with torch.cuda.device(ws.device):
             lib.reset_status(ws.data_ptr(), torch.cuda.current_stream(ws.device).cuda_stream)
 
+    def timeline(self, device):
+        """CTA 0's clock64 stamps of the last B200FA_FLAG_TIMELINE call as an int64
+        tensor [4 roles, TIMELINE_BLOCKS, 8 events] (synchronizes)."""
+        ws = self.workspace(torch.device(device))
+        torch.cuda.synchronize(ws.device)
+        raw = ws[lib.WS_TIMELINE_OFFSET:lib.WS_TIMELINE_OFFSET + lib.WS_TIMELINE_BYTES]
+        return raw.view(torch.int64).view(4, lib.TIMELINE_BLOCKS, 8).cpu()
+
     def trace(self, device) -> list[dict]:
         """Per-CTA trace records of the last traced call (synchronizes)."""
         ws = self.workspace(torch.device(device))
         torch.cuda.synchronize(ws.device)
-        raw = ws[lib.WS_HEADER_BYTES:].view(torch.int32).view(-1, 8).cpu()
+        raw = ws[lib.WS_HEADER_BYTES:lib.WS_TIMELINE_OFFSET].view(torch.int32).view(-1, 8).cpu()
         recs = []
         for r in raw.tolist():
             t0 = (r[2] & 0xFFFFFFFF) | ((r[3] & 0xFFFFFFFF) << 32)

@@ -76,10 +76,15 @@ extern "C" {
 
 /* Option flags (b200fa_options.flags). */
 #define B200FA_FLAG_TRACE          1u /* write one trace record per CTA        */
-/* Test-only: softmax warpgroup 1 withholds its first P-ready arrival, so the
- * MMA warp's bounded wait runs out and the kernel reports
- * B200FA_DEV_TIMEOUT.  Used by the failure-detection test only. */
+/* Test-only: the softmax warps of query tile 1 withhold their first
+ * P-ready arrival (keys 64-127), so the MMA warp's bounded wait runs out and
+ * the kernel reports B200FA_DEV_TIMEOUT.  Used by the failure-detection test
+ * only. */
 #define B200FA_FLAG_TEST_WITHHOLD_P 2u
+/* Debug: CTA 0 records SM-clock timestamps of its softmax, MMA and TMA
+ * threads for the first B200FA_TIMELINE_BLOCKS key blocks of its first work
+ * item into the timeline area of the workspace (pipeline analysis). */
+#define B200FA_FLAG_TIMELINE       4u
 
 typedef struct b200fa_options {
     uint32_t struct_size;   /* sizeof(b200fa_options)                        */
@@ -90,12 +95,20 @@ typedef struct b200fa_options {
 
 /* Workspace layout (bytes, 256-B aligned, zeroed once by the owner):
  *   [0, 256)       status header: u32 status, u32 site, u32 cta, u32 spare...
- *   [256, ...)     trace records, one per CTA (B200FA_FLAG_TRACE):
+ *   [256, 256 + 32 * B200FA_MAX_CTAS)
+ *                  trace records, one per CTA (B200FA_FLAG_TRACE):
  *                  {u32 smid, u32 items, u64 t_start_ns, u64 t_end_ns, u64 0}
+ *   [B200FA_WS_TIMELINE_OFFSET, + B200FA_WS_TIMELINE_BYTES)
+ *                  timeline (B200FA_FLAG_TIMELINE): u64 clock64 stamps,
+ *                  [role 0..3][block 0..B200FA_TIMELINE_BLOCKS-1][event 0..7],
+ *                  roles = softmax tile 0, softmax tile 1, MMA, TMA.
  * The status is sticky: it stays set until b200fa_reset_status. */
 #define B200FA_WS_HEADER_BYTES 256u
 #define B200FA_WS_TRACE_BYTES   32u
 #define B200FA_MAX_CTAS       1024
+#define B200FA_TIMELINE_BLOCKS  48u
+#define B200FA_WS_TIMELINE_OFFSET (B200FA_WS_HEADER_BYTES + B200FA_WS_TRACE_BYTES * B200FA_MAX_CTAS)
+#define B200FA_WS_TIMELINE_BYTES  (4u * B200FA_TIMELINE_BLOCKS * 8u * 8u)
 
 /* Number of work units: (b, hq, 128-row query block) triples, linearised as
  * ((b * Hq) + hq) * ceil(Nq / 128) + qb -- the order of the reference's

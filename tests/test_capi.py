@@ -77,7 +77,7 @@ def test_workspace_size_and_num_units():
     assert lib.num_units(2, 12, 131072) == 24576
     assert lib.num_units(1, 3, 130) == 6
     n = lib.workspace_size(1, 2, 1, 256, 256, 128, 0)
-    assert n == lib.WS_HEADER_BYTES + lib.WS_TRACE_BYTES * lib.MAX_CTAS
+    assert n == lib.WS_BYTES == lib.WS_TIMELINE_OFFSET + lib.WS_TIMELINE_BYTES
     with pytest.raises(lib.B200FAError):
         lib.workspace_size(1, 2, 1, 256, 256, 64, 0)
 

@@ -1,7 +1,7 @@
 """Failure detection on the GPU without a fault.
 
-The test-only flag B200FA_FLAG_TEST_WITHHOLD_P makes softmax warpgroup 1
-withhold its first P-ready arrival.  The MMA thread's bounded wait then
+The test-only flag B200FA_FLAG_TEST_WITHHOLD_P makes the softmax warps of
+query tile 1 withhold their first P-ready arrival (keys 64-127).  The MMA thread's bounded wait then
 runs out (limit set to 0.2 s here), the kernel records B200FA_DEV_TIMEOUT
 in its workspace status word, every role leaves its loop, TMEM is freed and
 the kernel returns.  The host reads the status; the context stays usable and
@@ -35,7 +35,7 @@ def test_bounded_wait_reports_timeout_and_context_survives():
     status = op.status(dev)
     assert status[0] == lib.DEV_TIMEOUT, status
     site_warp = status[1] >> 8
-    assert site_warp in (4, 5, 6, 7, 8), status  # softmax WG1 or the MMA warp gave up
+    assert 0 <= site_warp <= 8, status  # a softmax warp or the MMA warp gave up
 
     op.reset_status(dev)
     assert op.status(dev)[0] == lib.DEV_OK
