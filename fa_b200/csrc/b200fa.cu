@@ -25,11 +25,14 @@ using namespace b200fa;
 static_assert(kTimelineOffset == B200FA_WS_TIMELINE_OFFSET, "timeline offset mismatch");
 static_assert(kTimelineBlocks == int(B200FA_TIMELINE_BLOCKS), "timeline size mismatch");
 
-__global__ void __launch_bounds__(kThreads, 1) b200_fa_fp16_kernel(const __grid_constant__ FwdParams p) {
+// Clusters of two CTAs: the pair that shares every tensor-core product.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    b200_fa_fp16_kernel(const __grid_constant__ FwdParams p) {
   attention_fwd_body<0>(p);
 }
 
-__global__ void __launch_bounds__(kThreads, 1) b200_fa_fp32_kernel(const __grid_constant__ FwdParams p) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    b200_fa_fp32_kernel(const __grid_constant__ FwdParams p) {
   attention_fwd_body<1>(p);
 }
 
@@ -65,28 +68,52 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Per-device facts read once: SM count, kernel attributes set.
+// Per-device facts read once: kernel attributes set, and how many CTA pairs
+// can be resident at once (one per TPC whose two SMs are both available).
 struct DeviceState {
   std::once_flag once;
-  int sms = 0;
+  int pairs = 0;
   cudaError_t err = cudaSuccess;
 };
 DeviceState g_devices[64];
 
-int device_setup(int dev, int* sms) {
+int device_setup(int dev, int* pairs) {
   if (dev < 0 || dev >= 64) return fail(B200FA_ERR_OPTIONS, "device ordinal %d out of range", dev);
   DeviceState& d = g_devices[dev];
-  std::call_once(d.once, [&d, dev] {
-    cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(b200_fa_fp16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  std::call_once(d.once, [&d] {
+    cudaError_t e = cudaFuncSetAttribute(b200_fa_fp16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(b200_fa_fp32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2, 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = kSmemBytes;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      e = cudaOccupancyMaxActiveClusters(&d.pairs, b200_fa_fp16_kernel, &cfg);
+      if (e == cudaSuccess && d.pairs < 1) e = cudaErrorInvalidConfiguration;
+    }
     d.err = e;
   });
   if (d.err != cudaSuccess) return cuda_fail(d.err, "device setup");
-  *sms = d.sms;
+  *pairs = d.pairs;
   return B200FA_OK;
+}
+
+// Persistent grid: one CTA pair per resident slot, at most one per item;
+// `max_ctas` (when set) caps the CTAs, rounded down to whole pairs (>= 1).
+int grid_ctas(int pairs, int32_t max_ctas, int64_t items) {
+  int64_t n = pairs;
+  if (max_ctas > 0 && max_ctas / 2 < n) n = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
+  if (n > B200FA_MAX_CTAS / 2) n = B200FA_MAX_CTAS / 2;
+  if (items < n) n = items;
+  return int(2 * n);
 }
 
 int validate_shape(int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, int64_t Nk, int64_t D) {
@@ -103,12 +130,12 @@ int validate_shape(int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq, int64_t Nk, i
   return B200FA_OK;
 }
 
-int encode_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t planes) {
+int encode_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t planes, uint32_t box_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
   if (!fn) return fail(B200FA_ERR_NO_DRIVER, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[3] = {cuuint64_t(kHeadDim), cuuint64_t(rows), cuuint64_t(planes)};
   const cuuint64_t strides[2] = {cuuint64_t(kHeadDim * 2), cuuint64_t(rows) * kHeadDim * 2};
-  const cuuint32_t box[3] = {64, cuuint32_t(kBlockM), 1};
+  const cuuint32_t box[3] = {64, box_rows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -190,16 +217,16 @@ int b200fa_fwd_ex(const void* q, const void* k, const void* v, void* o, int64_t 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  int sms = 0;
-  rc = device_setup(dev, &sms);
+  int pairs = 0;
+  rc = device_setup(dev, &pairs);
   if (rc != B200FA_OK) return rc;
 
   FwdParams p;
   std::memset(&p, 0, sizeof(p));
-  if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv, kPairKeys)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv, kBlockN)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
   p.Hq = int32_t(Hq);
   p.Hkv = int32_t(Hkv);
   p.group = int32_t(Hq / Hkv);
@@ -214,10 +241,7 @@ int b200fa_fwd_ex(const void* q, const void* k, const void* v, void* o, int64_t 
   p.timeout_ns = uint64_t(opts->timeout_us ? opts->timeout_us : 2000000u) * 1000ull;
   p.ws = static_cast<uint32_t*>(workspace);
 
-  int grid = sms;
-  if (opts->max_ctas > 0 && opts->max_ctas < grid) grid = opts->max_ctas;
-  if (grid > B200FA_MAX_CTAS) grid = B200FA_MAX_CTAS;
-  if (items < grid) grid = int(items);
+  const int grid = grid_ctas(pairs, opts->max_ctas, items);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (variant == B200FA_VARIANT_FP16)
     b200_fa_fp16_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
@@ -320,8 +344,8 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  int sms = 0;
-  if ((rc = device_setup(dev, &sms)) != B200FA_OK) return rc;
+  int pairs = 0;
+  if ((rc = device_setup(dev, &pairs)) != B200FA_OK) return rc;
   void* scratch = nullptr;
   if ((rc = noalloc_scratch(dev, &scratch)) != B200FA_OK) return rc;
   if (scratch_out) *scratch_out = scratch;
@@ -329,10 +353,7 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
   const int64_t nqb = ceil_div<int64_t>(Nq, kBlockM);
   const int64_t items = plan_count<int64_t>(nqb, unit_begin, unit_end);
   if (items == 0) return B200FA_OK;
-  int grid = sms;
-  if (opts->max_ctas > 0 && opts->max_ctas < grid) grid = opts->max_ctas;
-  if (grid > B200FA_MAX_CTAS) grid = B200FA_MAX_CTAS;
-  if (items < grid) grid = int(items);
+  const int grid = grid_ctas(pairs, opts->max_ctas, items);
   const uint64_t need = (opts->flags & B200FA_FLAG_TIMELINE)
                             ? uint64_t(B200FA_WS_TIMELINE_OFFSET) + B200FA_WS_TIMELINE_BYTES
                             : uint64_t(B200FA_WS_HEADER_BYTES) +
@@ -346,10 +367,10 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
 
   FwdParams p;
   std::memset(&p, 0, sizeof(p));
-  if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv, kPairKeys)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv, kBlockN)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
   p.Hq = int32_t(Hq);
   p.Hkv = int32_t(Hkv);
   p.group = int32_t(Hq / Hkv);

@@ -3,9 +3,9 @@
 // allocation, MMA, TMEM loads/stores, commit) and a few ALU forms.
 //
 // Every wrapper is a direct spelling of one PTX instruction from the public
-// PTX ISA (8.7+, sm_100a).  None of them multicasts: TMA loads go to this
-// CTA's own shared memory only, so the same code is safe on any number of
-// GPUs.
+// PTX ISA (8.7+, sm_100a).  TMA loads go to this CTA's own shared memory
+// only and never multicast; the only multicast is the tcgen05.commit
+// arrival on the same mbarrier of both CTAs of a pair.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -120,20 +120,85 @@ __device__ __forceinline__ void regs_decrease() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
 }
 
+// ---------------------------------------------------------------- cluster
+// The kernel runs as clusters of two CTAs on the two SMs of a TPC (the
+// "pair"); rank 0 issues the pair's tensor-core work.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t num_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// All threads of both CTAs; release/acquire orders shared-memory writes
+// (barrier initialisation, TMEM address) across the pair.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// One arrival on an mbarrier anywhere in the cluster (release, cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// One relaxed arrival on an mbarrier anywhere in the cluster.  For hand-offs
+// whose data is already complete when the thread arrives (TMEM reads and
+// writes finished by tcgen05.wait::ld / wait::st): it skips the cluster-wide
+// release, which costs the arriving thread several hundred cycles.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Non-blocking probe with cluster-scope acquire: for barriers the other CTA
+// of the pair arrives on.
+__device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
-__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
-               "r"(ncols)
+// Pair (cta_group::2) forms: one warp with the same warp index in each CTA
+// allocates; the TMEM address is the same in both.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
                : "memory");
 }
 
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -144,79 +209,59 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (FP16 in, FP32 acc).
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                       uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16.
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                       uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// One 128x128x128 product as 8 K=16 steps in a single asm block, so the
-// issuing thread spends ~2 integer adds per MMA.  Descriptors are passed as
-// their low words (start-address field in bits 0-13, in 16-byte units) plus
-// the common high word; step kk adds a_step(kk)/b_step(kk) to the low words
-// (the field cannot carry: shared addresses are below 256 KiB).
-//   SS K-major operands (Q, K): step offset (kk/4)*1024 + (kk%4)*2  [16 B]
-//   TS with MN-major B (V):     step offset kk*128                 [16 B],
-//                               A (P in TMEM) advances 8 columns per step.
-// `first_acc` selects accumulate-into-D for step 0; later steps accumulate.
-__device__ __forceinline__ void mma_ss_k128(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
-                                            uint32_t idesc, uint32_t first_acc) {
+// S = A * B^T for the pair (M = 256: 128 rows of A from each CTA's shared
+// memory; B's N rows split in half between the CTAs, same offsets in both)
+// over a 128-wide K as 8 K=16 steps in one asm block.  Both operands are
+// K-major with 128-byte swizzle in two 64-column halves kAHalf / kBHalf
+// apart (16-byte units).  Descriptors are passed as their low words (start
+// address in bits 0-13, 16-byte units) plus the common high word; step kk
+// adds (kk/4)*kXHalf + (kk%4)*2 (no carry: shared addresses are below
+// 256 KiB).  Step 0 overwrites D.
+template <uint32_t kAHalf, uint32_t kBHalf>
+__device__ __forceinline__ void mma_pair_ss_k128(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
+                                                 uint32_t idesc) {
   asm volatile(
       "{\n\t"
       ".reg .b32 al, bl;\n\t"
       ".reg .b64 da, db;\n\t"
       ".reg .pred pf, pt;\n\t"
-      "setp.ne.b32 pf, %5, 0;\n\t"
+      "setp.ne.b32 pf, %4, %4;\n\t"
       "setp.eq.b32 pt, %4, %4;\n\t"
       "mov.b64 da, {%1, %3};\n\t"
       "mov.b64 db, {%2, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pf;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pf;\n\t"
       "add.u32 al, %1, 2;\n\t add.u32 bl, %2, 2;\n\t"
       "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
       "add.u32 al, %1, 4;\n\t add.u32 bl, %2, 4;\n\t"
       "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
       "add.u32 al, %1, 6;\n\t add.u32 bl, %2, 6;\n\t"
       "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, 1024;\n\t add.u32 bl, %2, 1024;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, %5;\n\t add.u32 bl, %2, %6;\n\t"
       "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, 1026;\n\t add.u32 bl, %2, 1026;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, %7;\n\t add.u32 bl, %2, %8;\n\t"
       "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, 1028;\n\t add.u32 bl, %2, 1028;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, %9;\n\t add.u32 bl, %2, %10;\n\t"
       "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, 1030;\n\t add.u32 bl, %2, 1030;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "add.u32 al, %1, %11;\n\t add.u32 bl, %2, %12;\n\t"
       "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, pt;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
       "}\n" ::"r"(d_tmem),
-      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(first_acc)
+      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "n"(kAHalf), "n"(kBHalf), "n"(kAHalf + 2), "n"(kBHalf + 2),
+      "n"(kAHalf + 4), "n"(kBHalf + 4), "n"(kAHalf + 6), "n"(kBHalf + 6)
       : "memory");
 }
 
-// Four K=16 steps (64 keys) of O += P * V: A from TMEM columns a_tmem + 8*i,
-// B = V rows 16*i.. at b_lo + 128*i.  `first_acc` applies to the first step.
-__device__ __forceinline__ void mma_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
-                                           uint32_t idesc, uint32_t first_acc) {
+// O (+)= P * V for the pair over 80 keys as 5 K=16 steps: A = P from each
+// CTA's TMEM (8 columns per step), B = V (MN-major, this CTA's 64 head-dim
+// columns; 16 keys = 2 KiB per step).  `first_acc` applies to step 0.
+__device__ __forceinline__ void mma_pair_ts_k80(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
+                                                uint32_t idesc, uint32_t first_acc) {
   asm volatile(
       "{\n\t"
       ".reg .b32 ta, bl;\n\t"
@@ -225,23 +270,49 @@ __device__ __forceinline__ void mma_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uin
       "setp.ne.b32 pf, %5, 0;\n\t"
       "setp.eq.b32 pt, %4, %4;\n\t"
       "mov.b64 db, {%2, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, pf;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], db, %4, pf;\n\t"
       "add.u32 ta, %1, 8;\n\t add.u32 bl, %2, 128;\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
       "add.u32 ta, %1, 16;\n\t add.u32 bl, %2, 256;\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
       "add.u32 ta, %1, 24;\n\t add.u32 bl, %2, 384;\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
+      "add.u32 ta, %1, 32;\n\t add.u32 bl, %2, 512;\n\t mov.b64 db, {bl, %3};\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
       "}\n" ::"r"(d_tmem),
       "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(first_acc)
       : "memory");
 }
 
-// Arrive once on `bar` when every tcgen05 operation issued so far by this
+// Arrive once on this CTA's `bar` when every pair MMA issued so far by this
 // thread has completed.
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// The same, arriving on `bar` in both CTAs of the pair (commit multicast;
+// an mbarrier arrival, not a data copy).
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((unsigned short)3)
+      : "memory");
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane -> r[0..15].
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// r[0..7] -> 8 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                : "memory");
 }
 

@@ -114,7 +114,10 @@ class Operator:
         return raw.view(torch.int64).view(4, lib.TIMELINE_BLOCKS, 8).cpu()
 
     def trace(self, device) -> list[dict]:
-        """Per-CTA trace records of the last traced call (synchronizes)."""
+        """Per-CTA trace records of the last traced call (synchronizes).
+
+        Both CTAs of a pair report the pair's item count; ``rank`` is the
+        CTA's rank in its pair."""
         ws = self.workspace(torch.device(device))
         torch.cuda.synchronize(ws.device)
         raw = ws[lib.WS_HEADER_BYTES:lib.WS_TIMELINE_OFFSET].view(torch.int32).view(-1, 8).cpu()
@@ -124,7 +127,7 @@ class Operator:
             t1 = (r[4] & 0xFFFFFFFF) | ((r[5] & 0xFFFFFFFF) << 32)
             if t1 == 0:
                 continue
-            recs.append({"smid": r[0], "items": r[1], "t_start_ns": t0, "t_end_ns": t1})
+            recs.append({"smid": r[0], "items": r[1], "t_start_ns": t0, "t_end_ns": t1, "rank": r[6]})
         return recs
 
 

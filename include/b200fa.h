@@ -76,10 +76,10 @@ extern "C" {
 
 /* Option flags (b200fa_options.flags). */
 #define B200FA_FLAG_TRACE          1u /* write one trace record per CTA        */
-/* Test-only: the softmax warps of query tile 1 withhold their first
- * P-ready arrival (keys 64-127), so the MMA warp's bounded wait runs out and
- * the kernel reports B200FA_DEV_TIMEOUT.  Used by the failure-detection test
- * only. */
+/* Test-only: the softmax warps of query tile 1 (in both CTAs of every
+ * pair) withhold their first P-ready arrival, so the MMA thread's bounded
+ * wait runs out and the kernel reports B200FA_DEV_TIMEOUT.  Used by the
+ * failure-detection test only. */
 #define B200FA_FLAG_TEST_WITHHOLD_P 2u
 /* Debug: CTA 0 records SM-clock timestamps of its softmax, MMA and TMA
  * threads for the first B200FA_TIMELINE_BLOCKS key blocks of its first work
@@ -90,14 +90,20 @@ typedef struct b200fa_options {
     uint32_t struct_size;   /* sizeof(b200fa_options)                        */
     uint32_t flags;         /* B200FA_FLAG_*                                  */
     uint32_t timeout_us;    /* bound of every device-side wait; 0 = 2 s       */
-    int32_t  max_ctas;      /* cap on the persistent grid; <= 0 = one per SM  */
+    int32_t  max_ctas;      /* cap on the persistent grid (CTAs; rounded down
+                               to whole pairs, at least one pair); <= 0 = one
+                               pair per TPC                                  */
 } b200fa_options;
 
 /* Workspace layout (bytes, 256-B aligned, zeroed once by the owner):
  *   [0, 256)       status header: u32 status, u32 site, u32 cta, u32 spare...
+ *                  site = (pair rank << 16) | (warp << 8) | barrier slot of
+ *                  the first wait that ran out
  *   [256, 256 + 32 * B200FA_MAX_CTAS)
  *                  trace records, one per CTA (B200FA_FLAG_TRACE):
- *                  {u32 smid, u32 items, u64 t_start_ns, u64 t_end_ns, u64 0}
+ *                  {u32 smid, u32 items, u64 t_start_ns, u64 t_end_ns,
+ *                   u32 pair rank, u32 0}; both CTAs of a pair count the
+ *                  pair's items
  *   [B200FA_WS_TIMELINE_OFFSET, + B200FA_WS_TIMELINE_BYTES)
  *                  timeline (B200FA_FLAG_TIMELINE): u64 clock64 stamps,
  *                  [role 0..3][block 0..B200FA_TIMELINE_BLOCKS-1][event 0..7],
@@ -161,7 +167,8 @@ int b200fa_reset_status(void* workspace, void* stream);
 const char* b200fa_kernel_name(int32_t variant);
 
 /* Host-side work-item plan (no GPU): item `index` of the range
- * [unit_begin, unit_end) as {bh, first q-block, count (1 or 2)}.  Returns
+ * [unit_begin, unit_end) as {bh, first q-block, count (1..4)}: up to four
+ * consecutive query blocks of one head, processed by one CTA pair.  Returns
  * the number of items, or a negative code. */
 int64_t b200fa_plan_item(int64_t B, int64_t Hq, int64_t Nq,
                          int64_t unit_begin, int64_t unit_end, int64_t index,

@@ -128,7 +128,10 @@ def test_trace_records_cover_the_grid():
     recs = op.trace(q.device)
     n_items = len(lib.plan_items(1, 12, 4096, 0, lib.num_units(1, 12, 4096)))
     sms = torch.cuda.get_device_properties(q.device).multi_processor_count
-    assert len(recs) == min(n_items, sms)
-    assert sum(r["items"] for r in recs) == n_items
+    pairs = len(recs) // 2
+    assert len(recs) == 2 * pairs and 1 <= pairs <= min(n_items, sms // 2)
+    assert sorted(r["rank"] for r in recs) == [0] * pairs + [1] * pairs
+    assert sum(r["items"] for r in recs if r["rank"] == 0) == n_items  # each item once per pair
+    assert sum(r["items"] for r in recs if r["rank"] == 1) == n_items
     assert all(r["t_end_ns"] > r["t_start_ns"] for r in recs)
     assert len({r["smid"] for r in recs}) == len(recs)  # one persistent CTA per SM
