@@ -24,16 +24,36 @@ using namespace b200fa;
 
 static_assert(kTimelineOffset == B200FA_WS_TIMELINE_OFFSET, "timeline offset mismatch");
 static_assert(kTimelineBlocks == int(B200FA_TIMELINE_BLOCKS), "timeline size mismatch");
+static_assert(kBlockN == B200FA_BLOCK_KEYS, "capture block size mismatch");
+static_assert(kFlagCapture == B200FA_FLAG_CAPTURE, "capture flag mismatch");
 
 // Clusters of two CTAs: the pair that shares every tensor-core product.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     b200_fa_fp16_kernel(const __grid_constant__ FwdParams p) {
-  attention_fwd_body<0>(p);
+  attention_fwd_body<0, false>(p);
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     b200_fa_fp32_kernel(const __grid_constant__ FwdParams p) {
-  attention_fwd_body<1>(p);
+  attention_fwd_body<1, false>(p);
+}
+
+// Debug-capture instantiations (B200FA_FLAG_CAPTURE).
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    b200_fa_fp16_capture_kernel(const __grid_constant__ FwdParams p) {
+  attention_fwd_body<0, true>(p);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    b200_fa_fp32_capture_kernel(const __grid_constant__ FwdParams p) {
+  attention_fwd_body<1, true>(p);
+}
+
+using KernelFn = void (*)(FwdParams);
+
+KernelFn kernel_for(int variant, bool capture) {
+  if (capture) return variant == B200FA_VARIANT_FP16 ? b200_fa_fp16_capture_kernel : b200_fa_fp32_capture_kernel;
+  return variant == B200FA_VARIANT_FP16 ? b200_fa_fp16_kernel : b200_fa_fp32_kernel;
 }
 
 namespace {
@@ -81,9 +101,12 @@ int device_setup(int dev, int* pairs) {
   if (dev < 0 || dev >= 64) return fail(B200FA_ERR_OPTIONS, "device ordinal %d out of range", dev);
   DeviceState& d = g_devices[dev];
   std::call_once(d.once, [&d] {
-    cudaError_t e = cudaFuncSetAttribute(b200_fa_fp16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(b200_fa_fp32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e = cudaSuccess;
+    for (int variant : {B200FA_VARIANT_FP16, B200FA_VARIANT_FP32})
+      for (bool capture : {false, true})
+        if (e == cudaSuccess)
+          e = cudaFuncSetAttribute(kernel_for(variant, capture), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kSmemBytes);
     if (e == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cudaLaunchAttribute attr[1];
@@ -146,6 +169,40 @@ int encode_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t planes, 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// The caller's options as a full struct: NULL means defaults, and the
+// 16-byte layout without the capture fields is accepted as well.
+constexpr uint32_t kOptionsV1Bytes = 16;
+int read_options(const b200fa_options* in, b200fa_options* out) {
+  *out = b200fa_options{sizeof(b200fa_options), 0u, 0u, 0, nullptr, 0};
+  if (in == nullptr) return B200FA_OK;
+  if (in->struct_size == sizeof(b200fa_options)) {
+    *out = *in;
+  } else if (in->struct_size == kOptionsV1Bytes) {
+    std::memcpy(out, in, kOptionsV1Bytes);
+    out->struct_size = sizeof(b200fa_options);
+    out->capture = nullptr;
+    out->capture_bytes = 0;
+  } else {
+    return fail(B200FA_ERR_OPTIONS, "b200fa_options.struct_size mismatch");
+  }
+  return B200FA_OK;
+}
+
+int64_t capture_bytes(int64_t B, int64_t Hq, int64_t Nq, int64_t Nk) {
+  // four scalar planes (m, l, alpha, z) + the O plane (kHeadDim floats per record)
+  return int64_t(4 + kHeadDim) * 4 * B * Hq * ceil_div<int64_t>(Nk, kBlockN) * Nq;
+}
+
+// Capture buffer checks (B200FA_FLAG_CAPTURE).
+int check_capture(const b200fa_options& o, int64_t B, int64_t Hq, int64_t Nq, int64_t Nk) {
+  if ((o.flags & B200FA_FLAG_CAPTURE) == 0) return B200FA_OK;
+  const uint64_t need = uint64_t(capture_bytes(B, Hq, Nq, Nk));
+  if (o.capture == nullptr || (reinterpret_cast<uintptr_t>(o.capture) & 15u) != 0 || o.capture_bytes < need)
+    return fail(B200FA_ERR_OPTIONS, "B200FA_FLAG_CAPTURE needs a 16-byte aligned buffer of at least %llu bytes",
+                (unsigned long long)need);
+  return B200FA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -207,9 +264,10 @@ int b200fa_fwd_ex(const void* q, const void* k, const void* v, void* o, int64_t 
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 || ws_bytes < ws_need)
     return fail(B200FA_ERR_WORKSPACE, "workspace must be 256-byte aligned and at least %llu bytes",
                 (unsigned long long)ws_need);
-  b200fa_options o_default{sizeof(b200fa_options), 0u, 0u, 0};
-  if (opts == nullptr) opts = &o_default;
-  if (opts->struct_size != sizeof(b200fa_options)) return fail(B200FA_ERR_OPTIONS, "b200fa_options.struct_size mismatch");
+  b200fa_options o_full;
+  if ((rc = read_options(opts, &o_full)) != B200FA_OK) return rc;
+  opts = &o_full;
+  if ((rc = check_capture(o_full, B, Hq, Nq, Nk)) != B200FA_OK) return rc;
   const int64_t nqb = ceil_div<int64_t>(Nq, kBlockM);
   const int64_t items = plan_count<int64_t>(nqb, unit_begin, unit_end);
   if (items == 0) return B200FA_OK;  // empty shard: nothing to launch
@@ -240,13 +298,13 @@ int b200fa_fwd_ex(const void* q, const void* k, const void* v, void* o, int64_t 
   p.flags = opts->flags;
   p.timeout_ns = uint64_t(opts->timeout_us ? opts->timeout_us : 2000000u) * 1000ull;
   p.ws = static_cast<uint32_t*>(workspace);
+  p.capture = (opts->flags & B200FA_FLAG_CAPTURE) ? opts->capture : nullptr;
+  p.heads = int32_t(B * Hq);
+  p.nq = int32_t(Nq);
 
   const int grid = grid_ctas(pairs, opts->max_ctas, items);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (variant == B200FA_VARIANT_FP16)
-    b200_fa_fp16_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
-  else
-    b200_fa_fp32_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
+  kernel_for(variant, p.capture != nullptr)<<<grid, kThreads, kSmemBytes, st>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   return B200FA_OK;
@@ -280,6 +338,11 @@ const char* b200fa_kernel_name(int32_t variant) {
   if (variant == B200FA_VARIANT_FP16) return "b200_fa_fp16_kernel";
   if (variant == B200FA_VARIANT_FP32) return "b200_fa_fp32_kernel";
   return nullptr;
+}
+
+int64_t b200fa_capture_bytes(int64_t B, int64_t Hq, int64_t Nq, int64_t Nk) {
+  if (B <= 0 || Hq <= 0 || Nq <= 0 || Nk <= 0) return fail(B200FA_ERR_SHAPE, "non-positive size");
+  return capture_bytes(B, Hq, Nq, Nk);
 }
 
 const char* b200fa_last_error_string(void) { return g_last_error; }
@@ -337,9 +400,10 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
                 (long long)unit_end, (long long)units);
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
     return fail(B200FA_ERR_ALIGNMENT, "tensor pointers must be 16-byte aligned");
-  b200fa_options o_default{sizeof(b200fa_options), 0u, 0u, 0};
-  if (opts == nullptr) opts = &o_default;
-  if (opts->struct_size != sizeof(b200fa_options)) return fail(B200FA_ERR_OPTIONS, "b200fa_options.struct_size mismatch");
+  b200fa_options o_full;
+  if ((rc = read_options(opts, &o_full)) != B200FA_OK) return rc;
+  opts = &o_full;
+  if ((rc = check_capture(o_full, B, Hq, Nq, Nk)) != B200FA_OK) return rc;
 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -384,16 +448,16 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
   p.flags = opts->flags;
   p.timeout_ns = uint64_t(opts->timeout_us ? opts->timeout_us : 2000000u) * 1000ull;
   p.ws = static_cast<uint32_t*>(scratch);
+  p.capture = (opts->flags & B200FA_FLAG_CAPTURE) ? opts->capture : nullptr;
+  p.heads = int32_t(B * Hq);
+  p.nq = int32_t(Nq);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The array keeps the previous call's contents: the status header must start
   // at zero for this call.  Trace records are rewritten by every CTA that runs.
   e = cudaMemsetAsync(scratch, 0, B200FA_WS_HEADER_BYTES, st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(noalloc status header)");
-  if (variant == B200FA_VARIANT_FP16)
-    b200_fa_fp16_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
-  else
-    b200_fa_fp32_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
+  kernel_for(variant, p.capture != nullptr)<<<grid, kThreads, kSmemBytes, st>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch (noalloc)");
   return B200FA_OK;

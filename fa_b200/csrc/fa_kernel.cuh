@@ -200,11 +200,15 @@ struct FwdParams {
   uint32_t flags;
   uint64_t timeout_ns;
   uint32_t* ws;             // status header + trace records
+  float* capture;           // capture kernels: [4][heads][n_kv][nq] + [heads][n_kv][nq][128] FP32
+  int32_t heads;            // B * Hq
+  int32_t nq;               // query rows per head
 };
 
 constexpr uint32_t kFlagTrace = 1u;
 constexpr uint32_t kFlagTestWithholdP = 2u;
 constexpr uint32_t kFlagTimeline = 4u;
+constexpr uint32_t kFlagCapture = 8u;
 
 // Debug timeline (kFlagTimeline): CTA 0 (rank 0 of the first pair) stamps
 // clock64() at fixed points of its first work item's first kTimelineBlocks
@@ -560,7 +564,9 @@ __device__ __forceinline__ float row_max80(const uint32_t* r) {
 
 // Softmax of one query tile per warpgroup (warps 0-3: tile 0, 4-7: tile 1),
 // one thread per query row (its TMEM lane), in both CTAs.
-template <int kVariant>  // 0 = FP16 softmax, 1 = FP32 softmax
+// kCapture: the debug-capture instantiation (separate kernels, so the
+// production ones carry no capture code).
+template <int kVariant, bool kCapture>  // kVariant 0 = FP16 softmax, 1 = FP32 softmax
 __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base, const Waiter& w,
                              uint32_t warp, uint32_t lane, uint32_t rank) {
   const int t = int(warp >> 2);   // tile = warpgroup
@@ -608,6 +614,22 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
     float m_ref = -INFINITY;  // reference maximum, log2 domain
     float l = 0.f;
     const Timeline tl = (wq == 0 && lane == 0) ? make_timeline(p, it) : Timeline{nullptr};
+    // Debug capture: cap_on is warp-uniform (this tile holds a unit of the
+    // item), cap_row per thread (its query row exists).  Record (b*Hq+hq,
+    // block j, row) sits at index (bh*n + j)*nq + row of each scalar plane
+    // (stride heads*n*nq) and, times 128, in the O plane after them.
+    bool cap_on = false, cap_row = false;
+    size_t cap_idx = 0;
+    if constexpr (kCapture) {
+      int bh, qb, cnt;
+      plan_decode<int>(p.nqb, p.unit_begin, p.unit_end, item, bh, qb, cnt);
+      const int u = 2 * t + int(rank);
+      const int qrow = (qb + u) * kBlockM + row;
+      cap_on = u < cnt;
+      cap_row = cap_on && qrow < p.nq;
+      cap_idx = (size_t(bh) * size_t(n)) * size_t(p.nq) + size_t(qrow);
+    }
+    const size_t cap_plane = size_t(p.heads) * size_t(n) * size_t(p.nq);
     for (int j = 0; j < n; ++j, ++g) {
       if (!w.wait(sm.bar(kBarSFull + t), g & 1u, site | (kBarSFull + t))) { ok = false; break; }
       tl.mark(t, j, 0);
@@ -669,7 +691,36 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       float a0, b0, a1, b1;
       f2_unpack(acc0, a0, b0);
       f2_unpack(acc1, a1, b1);
-      l += ((a0 + b0) + (a1 + b1)) + hsum;
+      const float z = ((a0 + b0) + (a1 + b1)) + hsum;
+      l += z;
+      if (kCapture && cap_on) {
+        const size_t idx = cap_idx + size_t(j) * size_t(p.nq);
+        if (cap_row) {
+          float* rec = p.capture + idx;
+          rec[0] = m_ref;
+          rec[cap_plane] = l;
+          rec[2 * cap_plane] = j == 0 ? 0.f : alpha;
+          rec[3 * cap_plane] = z;
+        }
+        // O after PV_t(j) (unnormalised FP32, relative to m_ref): wait for
+        // that product, read the row from TMEM (whole warp), store it.
+        if (!pv_done_upto(g + 1)) { ok = false; break; }
+        tc_fence_after();
+        float4* orec = reinterpret_cast<float4*>(p.capture + 4 * cap_plane + idx * size_t(kHeadDim));
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * c, o);
+          tmem_wait_ld();
+          if (cap_row) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              orec[8 * c + u] = make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]),
+                                            __uint_as_float(o[4 * u + 2]), __uint_as_float(o[4 * u + 3]));
+          }
+        }
+        tc_fence_before();
+      }
     }
     if (!ok) break;
 
@@ -718,7 +769,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
   if (wq == 0 && lane == 0) bulk_wait_group0();
 }
 
-template <int kVariant>
+template <int kVariant, bool kCapture>
 __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
@@ -770,7 +821,7 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
 
   if (warp < 8) {
     regs_increase<kSoftmaxRegs>();
-    softmax_role<kVariant>(p, sm, tmem_base, w, warp, lane, rank);
+    softmax_role<kVariant, kCapture>(p, sm, tmem_base, w, warp, lane, rank);
   } else {
     regs_decrease<kControlRegs>();
     if (lane == 0) {

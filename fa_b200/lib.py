@@ -23,6 +23,8 @@ VARIANTS = {"fp16": VARIANT_FP16, "fp32": VARIANT_FP32}
 FLAG_TRACE = 1
 FLAG_TEST_WITHHOLD_P = 2
 FLAG_TIMELINE = 4
+FLAG_CAPTURE = 8
+BLOCK_KEYS = 80
 
 DEV_OK = 0
 DEV_TIMEOUT = 1
@@ -42,7 +44,8 @@ _i64, _i32, _u32, _u64, _p, _f = C.c_int64, C.c_int32, C.c_uint32, C.c_uint64, C
 
 class Options(C.Structure):
     _fields_ = [("struct_size", C.c_uint32), ("flags", C.c_uint32),
-                ("timeout_us", C.c_uint32), ("max_ctas", C.c_int32)]
+                ("timeout_us", C.c_uint32), ("max_ctas", C.c_int32),
+                ("capture", C.c_void_p), ("capture_bytes", C.c_uint64)]
 
 
 SIGNATURES = {
@@ -58,6 +61,7 @@ SIGNATURES = {
     "b200fa_kernel_name": (C.c_char_p, [_i32]),
     "b200fa_plan_item": (_i64, [_i64, _i64, _i64, _i64, _i64, _i64,
                                 C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]),
+    "b200fa_capture_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "b200fa_last_error_string": (C.c_char_p, []),
     "b200fa_version": (C.c_char_p, []),
     "b200fa_fwd_noalloc": (C.c_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i32,
@@ -148,12 +152,20 @@ def kernel_name(variant: int) -> str:
 
 
 def fwd(q_ptr, k_ptr, v_ptr, o_ptr, B, Hq, Hkv, Nq, Nk, D, scale, variant,
-        unit_begin, unit_end, ws_ptr, ws_bytes, stream, *, flags=0, timeout_us=0, max_ctas=0):
+        unit_begin, unit_end, ws_ptr, ws_bytes, stream, *, flags=0, timeout_us=0, max_ctas=0,
+        capture_ptr=None, capture_bytes=0):
     """Raw pointer call of b200fa_fwd_ex; raises B200FAError on a nonzero status."""
-    opts = Options(C.sizeof(Options), flags, timeout_us, max_ctas)
+    opts = Options(C.sizeof(Options), flags, timeout_us, max_ctas, capture_ptr, capture_bytes)
     status = load().b200fa_fwd_ex(q_ptr, k_ptr, v_ptr, o_ptr, B, Hq, Hkv, Nq, Nk, D, scale, variant,
                                   unit_begin, unit_end, ws_ptr, ws_bytes, stream, C.byref(opts))
     check(status, "b200fa_fwd")
+
+
+def capture_bytes(B, Hq, Nq, Nk) -> int:
+    """Size of the B200FA_FLAG_CAPTURE buffer (four FP32 planes)."""
+    n = int(load().b200fa_capture_bytes(B, Hq, Nq, Nk))
+    check(n if n < 0 else 0, "b200fa_capture_bytes")
+    return n
 
 
 def read_status(ws_ptr, stream) -> tuple[int, int, int, int]:

@@ -75,7 +75,11 @@ class Operator:
         return ws
 
     def __call__(self, q, k, v, *, scale: float | None = None, out: torch.Tensor | None = None,
-                 unit_range: tuple[int, int] | None = None, flags: int = 0) -> torch.Tensor:
+                 unit_range: tuple[int, int] | None = None, flags: int = 0,
+                 capture: torch.Tensor | None = None) -> torch.Tensor:
+        """O = softmax(Q K^T * scale) V.  ``capture`` (FP32, at least
+        ``capture_bytes(...)`` bytes, on Q's device) turns on the debug
+        capture of the per-block online-softmax state (``capture_view``)."""
         B, Hq, Hkv, Nq, Nk = _geometry(q, k, v)
         if out is None:
             out = torch.empty_like(q)
@@ -86,13 +90,47 @@ class Operator:
         begin, end = (0, units) if unit_range is None else (int(unit_range[0]), int(unit_range[1]))
         scale = float(HEAD_DIM ** -0.5 if scale is None else scale)
         ws = self.workspace(q.device)
+        cap_ptr, cap_bytes, cap_flag = None, 0, 0
+        if capture is not None:
+            if capture.dtype != torch.float32 or not capture.is_contiguous() or capture.device != q.device:
+                raise ValueError("capture must be a contiguous FP32 tensor on Q's device")
+            cap_ptr, cap_bytes, cap_flag = capture.data_ptr(), capture.numel() * 4, lib.FLAG_CAPTURE
         with torch.cuda.device(q.device):
             stream = torch.cuda.current_stream(q.device).cuda_stream
             lib.fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                     B, Hq, Hkv, Nq, Nk, HEAD_DIM, scale, self.variant_id, begin, end,
                     ws.data_ptr(), ws.numel(), stream,
-                    flags=self.flags | flags, timeout_us=self.timeout_us, max_ctas=self.max_ctas)
+                    flags=self.flags | flags | cap_flag, timeout_us=self.timeout_us, max_ctas=self.max_ctas,
+                    capture_ptr=cap_ptr, capture_bytes=cap_bytes)
         return out
+
+    CAPTURE_LIMIT = 256 << 20  # bytes; the reference restricts its capture the same way
+
+    @staticmethod
+    def capture_buffer(q, k) -> torch.Tensor:
+        """A NaN-filled capture buffer for Q/K's shapes (entries outside the
+        unit range stay NaN).  Debug capture is for small inputs only."""
+        B, Hq, Nq, _ = q.shape
+        nbytes = lib.capture_bytes(B, Hq, Nq, k.shape[2])
+        if nbytes > Operator.CAPTURE_LIMIT:
+            raise ValueError("debug capture is restricted to small inputs (at most 256 MiB)")
+        return torch.full((nbytes // 4,), float("nan"), dtype=torch.float32, device=q.device)
+
+    @staticmethod
+    def capture_view(capture: torch.Tensor, q, k) -> dict:
+        """The capture buffer as {m, l, alpha, z: [B, Hq, n_blocks, Nq];
+        o, o_partial: [B, Hq, n_blocks, Nq, D]}.  ``o`` is the running
+        (unnormalised) output after each key block; ``o_partial`` the block's
+        own P V product, O_j - alpha_j O_(j-1), derived here."""
+        B, Hq, Nq, D = q.shape
+        nb = -(-k.shape[2] // lib.BLOCK_KEYS)
+        rows = B * Hq * nb * Nq
+        planes = capture[:4 * rows].view(4, B, Hq, nb, Nq)
+        o = capture[4 * rows:4 * rows + rows * D].view(B, Hq, nb, Nq, D)
+        prev = torch.cat([torch.zeros_like(o[:, :, :1]), o[:, :, :-1]], dim=2)
+        o_partial = o - planes[2].unsqueeze(-1) * prev
+        return {"m": planes[0], "l": planes[1], "alpha": planes[2], "z": planes[3],
+                "o": o, "o_partial": o_partial}
 
     def status(self, device) -> tuple[int, int, int, int]:
         """Synchronize and read the device status header {status, site, cta, 0}."""

@@ -85,14 +85,39 @@ extern "C" {
  * threads for the first B200FA_TIMELINE_BLOCKS key blocks of its first work
  * item into the timeline area of the workspace (pipeline analysis). */
 #define B200FA_FLAG_TIMELINE       4u
+/* Debug capture (the counterpart of the reference's `capture` attribute,
+ * binding.py:39-41, vector_output.h:94-106): per key block and query row the
+ * kernel writes its online-softmax state into b200fa_options.capture, FP32,
+ * laid out [plane][b*Hq + hq][key block][query row] with planes
+ *   0  m      reference maximum after the block (log2 domain: scores times
+ *             scale*log2(e)); it moves only when a block maximum exceeds it
+ *             by more than 8 (lazy rescaling)
+ *   1  l      running row sum after the block, relative to m
+ *   2  alpha  factor applied to l and O at this block (2^(m_old - m_new);
+ *             1 when m did not move, 0 at the first block)
+ *   3  z      the block's own row sum, relative to m
+ * followed by the O plane, [b*Hq + hq][key block][query row][128]:
+ *   O after the block's P V product (unnormalised, relative to m); the
+ *   block's own partial product is O_j - alpha_j * O_(j-1).
+ * The reference's capture holds the same (m, l, alpha, z, O) per packet.
+ * Key blocks are B200FA_BLOCK_KEYS keys wide.  Rows of the unit range only;
+ * other entries are left untouched.  The buffer must be 16-byte aligned;
+ * size: b200fa_capture_bytes() = 528 * B * Hq * ceil(Nk / 80) * Nq.  The
+ * capture serialises each block's softmax with its P V product: a debug
+ * mode, not a fast path. */
+#define B200FA_FLAG_CAPTURE        8u
+#define B200FA_BLOCK_KEYS         80
 
 typedef struct b200fa_options {
-    uint32_t struct_size;   /* sizeof(b200fa_options)                        */
+    uint32_t struct_size;   /* sizeof(b200fa_options); 16 (no capture fields)
+                               is accepted too                               */
     uint32_t flags;         /* B200FA_FLAG_*                                  */
     uint32_t timeout_us;    /* bound of every device-side wait; 0 = 2 s       */
     int32_t  max_ctas;      /* cap on the persistent grid (CTAs; rounded down
                                to whole pairs, at least one pair); <= 0 = one
                                pair per TPC                                  */
+    float*   capture;       /* B200FA_FLAG_CAPTURE: device buffer             */
+    uint64_t capture_bytes; /* its size, >= b200fa_capture_bytes(...)        */
 } b200fa_options;
 
 /* Workspace layout (bytes, 256-B aligned, zeroed once by the owner):
@@ -173,6 +198,10 @@ const char* b200fa_kernel_name(int32_t variant);
 int64_t b200fa_plan_item(int64_t B, int64_t Hq, int64_t Nq,
                          int64_t unit_begin, int64_t unit_end, int64_t index,
                          int64_t* bh, int64_t* qblock, int64_t* count);
+
+/* Bytes of the B200FA_FLAG_CAPTURE buffer: 16 * B * Hq * ceil(Nk / 80) * Nq
+ * (four FP32 planes).  Negative on invalid sizes. */
+int64_t b200fa_capture_bytes(int64_t B, int64_t Hq, int64_t Nq, int64_t Nk);
 
 /* Description of the last error on the calling thread ("" if none). */
 const char* b200fa_last_error_string(void);

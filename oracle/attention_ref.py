@@ -19,6 +19,8 @@ What it restates
   the most exact statement of the operator, used to pin the FP32 one.
 * ``attention_rows_fp32`` -- selected query rows only, for spot checks of
   full-size problems.
+* ``online_state_f64`` -- the per-block online-softmax state (m, l, alpha,
+  z, O) that the kernel's debug capture records, in float64.
 * ``attention_sdpa_fp32`` -- the reference formula in its own form
   (repeat_interleave + FP32 ``scaled_dot_product_attention``): the CPU path
   that bench.py times as the CPU baseline.
@@ -109,6 +111,61 @@ def attention_f64(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float | No
             s -= s.max(axis=-1, keepdims=True)
             p = np.exp(s)
             out[b, h] = (p @ vf) / p.sum(axis=-1, keepdims=True)
+    return out
+
+
+def online_state_f64(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float | None = None,
+                     block: int = 80, threshold: float = 8.0) -> dict:
+    """float64 restatement of the per-block online-softmax state that the
+    debug capture records, for small cases.
+
+    The recurrence is the reference's (CCE ``Stats``,
+    op_kernel/vector_output.h:94-106 of the cce_fa_nqkq_nz_resident backend:
+    l = z at the first packet, l = alpha*l + z after it; O likewise), here
+    over key blocks of ``block`` keys with the lazy reference maximum of the
+    B200 kernel: in the log2 domain (scores times scale*log2(e)) the maximum
+    m moves to a block's maximum only when that exceeds m by more than
+    ``threshold``; then alpha = 2^(m_old - m_new) (0 at the first block),
+    else alpha = 1.  Per block: z = sum 2^(s - m) over the block's keys,
+    l = alpha*l + z, O = alpha*O + fp16(2^(s - m)) V (P is rounded to FP16
+    before the P V product, as the kernel does).
+
+    Returns {m, l, alpha, z: [B, Hq, n_blocks, Nq]; o: [..., D];
+    margin: [B, Hq, Nq]} where margin is the smallest distance of a
+    block maximum from the move threshold (a decision closer than the
+    arithmetic's error may go either way).
+    """
+    B, Hq, Nq, D = q.shape
+    Nk = k.shape[2]
+    G = Hq // k.shape[1]
+    scale = D ** -0.5 if scale is None else scale
+    nb = -(-Nk // block)
+    log2e = 1.0 / np.log(2.0)
+    out = {name: np.empty((B, Hq, nb, Nq)) for name in ("m", "l", "alpha", "z")}
+    out["o"] = np.empty((B, Hq, nb, Nq, D))
+    out["margin"] = np.full((B, Hq, Nq), np.inf)
+    for b in range(B):
+        for h in range(Hq):
+            s = (q[b, h].astype(np.float64) @ k[b, h // G].astype(np.float64).T) * (scale * log2e)
+            vf = v[b, h // G].astype(np.float64)
+            m = np.full(Nq, -np.inf)
+            l = np.zeros(Nq)
+            o = np.zeros((Nq, D))
+            for j in range(nb):
+                sb = s[:, j * block:(j + 1) * block]
+                m_blk = sb.max(axis=1)
+                gap = m_blk - (m + threshold)
+                out["margin"][b, h] = np.minimum(out["margin"][b, h], np.abs(gap))
+                move = gap > 0
+                alpha = np.where(move, np.exp2(np.where(move, m - m_blk, 0.0)), 1.0)
+                m = np.where(move, m_blk, m)
+                p = np.exp2(sb - m[:, None])
+                z = p.sum(axis=1)
+                l = alpha * l + z
+                o = alpha[:, None] * o + p.astype(np.float16).astype(np.float64) @ vf[j * block:(j + 1) * block]
+                out["m"][b, h, j], out["l"][b, h, j], out["z"][b, h, j] = m, l, z
+                out["alpha"][b, h, j] = 0.0 if j == 0 else alpha
+                out["o"][b, h, j] = o
     return out
 
 

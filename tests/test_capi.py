@@ -118,3 +118,25 @@ def test_status_calls_reject_null():
     out = (C.c_uint32 * 4)()
     assert lib.load().b200fa_read_status(None, None, out) == -1
     assert lib.load().b200fa_reset_status(None, None) == -1
+
+
+def _fwd_ex(flags, capture, capture_bytes):
+    opts = lib.Options(C.sizeof(lib.Options), flags, 0, 0, capture, capture_bytes)
+    return lib.load().b200fa_fwd_ex(16, 16, 16, 16, 1, 2, 1, 300, 1000, 128, 0.088, 0, 0, 6,
+                                    256, 1 << 20, None, C.byref(opts))
+
+
+def test_capture_size_and_validation_without_gpu():
+    # four FP32 planes + the 128-float O plane per (b*Hq+hq, key block, query row)
+    need = lib.capture_bytes(1, 2, 300, 1000)
+    assert need == 528 * 2 * 13 * 300
+    with pytest.raises(lib.B200FAError):
+        lib.capture_bytes(0, 2, 300, 1000)
+    assert _fwd_ex(lib.FLAG_CAPTURE, None, need) == -11      # no buffer
+    assert _fwd_ex(lib.FLAG_CAPTURE, 4096 + 4, need) == -11  # not 16-byte aligned
+    assert _fwd_ex(lib.FLAG_CAPTURE, 4096, need - 1) == -11  # too small
+    assert "capture" in lib.last_error().lower()
+    # the legacy 16-byte options layout (no capture fields) is still accepted
+    legacy = lib.Options(16, 0, 0, 0, None, 0)
+    assert lib.load().b200fa_fwd_ex(16, 16, 16, 16, 1, 2, 1, 300, 1000, 128, 0.088, 0, 2, 2,
+                                    256, 1 << 20, None, C.byref(legacy)) == 0

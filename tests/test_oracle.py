@@ -14,7 +14,8 @@ import numpy as np
 import pytest
 import torch
 
-from oracle.attention_ref import attention_f64, attention_fp32, attention_rows_fp32, attention_sdpa_fp32
+from oracle.attention_ref import (attention_f64, attention_fp32, attention_rows_fp32, attention_sdpa_fp32,
+                                  online_state_f64)
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 META = json.loads((GOLDEN / "cases.json").read_text())
@@ -102,3 +103,33 @@ def test_canonical_inputs_match_reference_generator_on_cpu():
             assert t[n].dtype == torch.float16
             assert float(t[n].double().sum()) == chk[f"{n}_sum"]
             assert [float(x) for x in t[n].flatten()[:4]] == chk[f"{n}_head"]
+
+
+@pytest.mark.parametrize("Nk,kscale", [(80, 1.0), (250, 1.0), (401, 4.0)])
+def test_online_state_recurrence(Nk, kscale):
+    """The per-block state restatement (what the debug capture is checked
+    against) is consistent: l_j = alpha_j l_(j-1) + z_j, alpha_0 = 0, m never
+    decreases and moves only past the threshold, the final (m, l) give the
+    row's log-sum-exp, and O/l is the attention output (FP16 P rounding)."""
+    rng = np.random.default_rng(Nk)
+    q = rng.standard_normal((1, 2, 40, 128)).astype(np.float16)
+    k = (rng.standard_normal((1, 1, Nk, 128)) * kscale).astype(np.float16)
+    v = rng.standard_normal((1, 1, Nk, 128)).astype(np.float16)
+    st = online_state_f64(q, k, v)
+    m, l, alpha, z = st["m"], st["l"], st["alpha"], st["z"]
+    nb = -(-Nk // 80)
+    assert m.shape == (1, 2, nb, 40) and st["o"].shape == (1, 2, nb, 40, 128)
+    assert np.all(alpha[:, :, 0] == 0)
+    assert np.all((alpha[:, :, 1:] > 0) & (alpha[:, :, 1:] <= 1))
+    dm = np.diff(m, axis=2)
+    assert np.all(dm >= 0)
+    assert np.all((dm == 0) | (dm > 8.0))
+    assert np.all((alpha[:, :, 1:] == 1) == (dm == 0))
+    np.testing.assert_allclose(l[:, :, 0], z[:, :, 0], rtol=0)
+    np.testing.assert_allclose(l[:, :, 1:], alpha[:, :, 1:] * l[:, :, :-1] + z[:, :, 1:], rtol=1e-13)
+    assert np.all(z <= 80 * 2.0 ** 8)
+    s = (q[0].astype(np.float64) @ k[0, 0].astype(np.float64).T) * (128 ** -0.5 / np.log(2.0))
+    lse2 = np.log2(np.exp2(s - s.max(-1, keepdims=True)).sum(-1)) + s.max(-1)
+    np.testing.assert_allclose(m[0, :, -1] + np.log2(l[0, :, -1]), lse2, rtol=0, atol=1e-12)
+    o = st["o"][:, :, -1] / l[:, :, -1, :, None]
+    assert np.abs(o - attention_f64(q, k, v)).max() < 2e-3
