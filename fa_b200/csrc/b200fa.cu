@@ -282,7 +282,7 @@ int b200fa_fwd_ex(const void* q, const void* k, const void* v, void* o, int64_t 
   FwdParams p;
   std::memset(&p, 0, sizeof(p));
   if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv, kPairKeys)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv, kKBoxRows)) != B200FA_OK) return rc;
   if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv, kBlockN)) != B200FA_OK) return rc;
   if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
   p.Hq = int32_t(Hq);
@@ -432,7 +432,7 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
   FwdParams p;
   std::memset(&p, 0, sizeof(p));
   if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv, kPairKeys)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv, kKBoxRows)) != B200FA_OK) return rc;
   if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv, kBlockN)) != B200FA_OK) return rc;
   if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
   p.Hq = int32_t(Hq);

@@ -15,11 +15,11 @@
 // The pair.  Both tensor-core products run as pair MMAs (tcgen05
 // cta_group::2, M = 256) issued by rank 0: each CTA holds 128 query rows of
 // a tile, and the B operand is split between the two shared memories --
-// rank r holds keys [40r, 40r+40) of every 80-key K block (S = Q K^T) and
+// rank r holds keys [64r, 64r+64) of every 128-key K block (S = Q K^T) and
 // head-dim columns [64r, 64r+64) of every V block (O = P V).  Per SM and
-// K=16 step the QK product then reads 4 KiB of Q and 1.25 KiB of K from
-// shared memory (41 cycles at 128 B/clk against 40 cycles of tensor work),
-// and each SM loads only half of every K/V block.
+// K=16 step the QK product then reads 4 KiB of Q and 2 KiB of K from shared
+// memory (48 cycles at 128 B/clk against 64 cycles of tensor work), and each
+// SM loads only half of every K/V block.
 //
 // CTA roles (384 threads = 3 warpgroups), the same in both CTAs:
 //   warps 0-3   softmax, query tile 0 (TMEM lanes = rows)
@@ -36,35 +36,47 @@
 // products keep the pipe busy while the other tile's issuer waits.
 //
 // Tensor memory, per tile t (same columns in both CTAs):
-//   O_t [128t, 128t+128)     FP32 output accumulator
-//   S_t [256+128t, +80)      FP32 scores of the current key block
-//   P_t [336+128t, +40)      FP16 probabilities (pairs), A operand of PV
-// S and P are separate, so the next S of a tile is computed while its
-// softmax still works on the previous block.
+//   S_t [128t, 128t+128)     FP32 scores of the current 128-key block, as
+//                            two halves: keys 0-63 in columns [0,64), keys
+//                            64-127 in [64,128).  Once the softmax has read
+//                            them, P_t (FP16 pairs) takes columns [96,128)
+//                            (keys 0-63) and [64,96) (keys 64-127)
+//   O_t [256+128t, +128)     FP32 output accumulator
 //
 // Shared memory (1024-B aligned, 128-byte swizzle as the TMA writes it):
 //   Q0, Q1 (2 x 32 KiB: two 64-column halves of 128 rows; each also stages
-//   its tile's FP16 output for the TMA store), a ring of kStages 10 KiB
-//   stages holding this CTA's half of K_j (two 64-column boxes of 40 rows)
-//   and of V_j (one box of 80 rows x 64 columns) alternately, mbarriers.
+//   its tile's FP16 output for the TMA store), a ring of kStages 16 KiB
+//   stages holding this CTA's part of K_j (32 keys of each S half, as two
+//   64-column boxes of 32 rows per half) and of V_j (one box of 128 rows x
+//   64 columns) alternately, mbarriers.
 //
-// Per key block j the issuer of tile t issues S_t(j+1), commits "S full t"
-// in both CTAs, issues PV_t(j) and commits "P free t" in both CTAs.
-// S_t(j+1) waits until all 8 softmax warps of tile t (4 per CTA) have read
-// S_t(j) ("S free"); PV_t(j) waits for their P_t(j) ("P full").  The
-// softmax starts block j+1 as soon as its scores are in TMEM and waits for
-// PV_t(j) only before it rescales O_t or overwrites P_t.  The softmax of
-// each tile releases its use of the K/V ring slots locally (K_j once "S
-// full" j, V_j once "P free" j completed); a slot is refilled after both
-// tiles released it.  Rank 1's TMA completions reach
-// rank 0 through its warp 11, which waits for each local stage and arrives
-// on rank 0's barrier: no copy ever signals the other CTA.
+// Per key block j the issuer of tile t works in two windows.  After "P
+// half" j (all 8 softmax warps of the tile, 4 per CTA, have read S_t(j) and
+// written P_t(j) keys 0-63): S_t(j+1) keys 0-63 ("S low" j+1, its columns
+// hold no P), then PV over keys 0-63.  After "P full" j (keys 64-127
+// written): PV over keys 64-127, then S_t(j+1) keys 64-127 ("S high" j+1)
+// over the columns both PV halves read -- one thread issues them, and the
+// tensor pipe executes its products in order.  So S_t(j+1) keys 0-63 are
+// computed while the softmax still works on block j, and the ordering gives
+// the softmax its guarantees without further waits: "S high" j+1 means the
+// PV of block j is complete, so O_t may be rescaled and P_t(j+1) written.
+// Splitting S costs shared-memory bandwidth (an N = 64 half reads Q once
+// per 32 tensor cycles: 40 cycles at 128 B/clk) and buys S(j+1) keys 0-63
+// off the softmax's path.  The softmax releases its use of the K/V ring
+// slots locally (K_j once "S high" j, V_j once "S high" j+1 or, for the
+// item's last block, "O final"); a slot is refilled after both tiles
+// released it.  Rank 1's TMA completions reach rank 0 through its warp 11,
+// which waits for each local stage and arrives on rank 0's barrier: no copy
+// ever signals the other CTA.
 //
 // Online softmax (per query row, one thread per row): running reference
 // maximum m (log2 domain), running sum l.  The reference moves only when a
 // block's maximum exceeds it by more than kRescaleLog2 (lazy rescaling), so
 // P <= 2^kRescaleLog2 and O/l is exact at the end whatever the reference.
-// When it moves, the warp rescales its 32 rows of O in TMEM.
+// When it moves, the warp rescales its 32 rows of O in TMEM.  After a
+// tile's first block the exponentials of keys 0-63 are computed against the
+// current reference while keys 64-127 are loaded and reduced, and redone in
+// the rare block where the reference moves.
 //
 // Every wait is bounded (global timer); on expiry the kernel records
 // B200FA_DEV_TIMEOUT in the workspace, raises the abort flag of both CTAs,
@@ -78,16 +90,18 @@
 namespace b200fa {
 
 constexpr int kBlockM = 128;    // query rows per tile (per CTA)
-constexpr int kBlockN = 80;     // keys per KV block
+constexpr int kBlockN = 128;    // keys per KV block
 constexpr int kHeadDim = 128;   // head dimension (fixed)
 constexpr int kPairKeys = kBlockN / 2;    // K rows of a block held by each CTA
 constexpr int kPairDims = kHeadDim / 2;   // V head-dim columns held by each CTA
 constexpr int kItemUnits = 4;   // query units per work item (2 tiles x 2 CTAs)
-constexpr int kStages = 14;     // K/V ring depth (even: a slot only ever holds K or only V)
+constexpr int kStages = 10;     // K/V ring depth (even: a slot only ever holds K or only V)
 constexpr int kQTileBytes = kBlockM * kHeadDim * 2;   // 32 KiB
 constexpr int kQHalfBytes = kQTileBytes / 2;          // TMA box: 64 cols x 128 rows
-constexpr int kKHalfBytes = kPairKeys * 128;          // TMA box: 64 cols x 40 rows
-constexpr int kStageBytes = 2 * kKHalfBytes;          // 10 KiB
+constexpr int kKBoxRows = kPairKeys / 2;             // K rows of one S half held by each CTA
+constexpr int kKBoxBytes = kKBoxRows * 128;           // TMA box: 64 cols x 32 rows
+constexpr int kKPartBytes = 2 * kKBoxBytes;           // one S half's keys, all 128 columns
+constexpr int kStageBytes = 2 * kKPartBytes;          // 16 KiB
 static_assert(kBlockN * kPairDims * 2 == kStageBytes, "K and V stages must have the same size");
 static_assert(kStages % 2 == 0, "ring slots must alternate K and V consistently");
 constexpr int kThreads = 384;    // 3 warpgroups
@@ -104,24 +118,26 @@ constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (factor 256)
 
 // Tensor memory columns.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemO = 0;       // + 128 t
-constexpr uint32_t kTmemS = 256;     // + 128 t
-constexpr uint32_t kTmemP = 336;     // + 128 t
-static_assert(kTmemP + 128 + kBlockN / 2 <= kTmemCols, "TMEM budget");
+constexpr uint32_t kTmemS = 0;       // + 128 t
+constexpr uint32_t kTmemO = 256;     // + 128 t
+constexpr uint32_t kTmemPLo = 96;    // column offset within S_t of P for keys 0-63
+constexpr uint32_t kTmemPHi = 64;    // column offset within S_t of P for keys 64-127
+static_assert(kTmemO + 256 <= kTmemCols, "TMEM budget");
 
 // Barrier slots.  "rank 0" barriers are only waited on in rank 0.
 constexpr int kBarQFull = 0;     // [2] Q tile landed (rank 0: own TMA + rank 1's forward; rank 1: own TMA)
 constexpr int kBarQEmpty = 2;    // [2] Q buffer free (epilogue store read it)                    local
-constexpr int kBarSFull = 4;     // [2] S_t of a block computed     (pair commit to both CTAs)
-constexpr int kBarSFree = 6;     // [2] rank 0: S_t read by the 8 softmax warps of tile t
-constexpr int kBarPFull = 8;     // [2] rank 0: P_t written by the 8 softmax warps of tile t
+constexpr int kBarSLo = 4;       // [2] S_t keys 0-63 of a block computed   (pair commit to both CTAs)
+constexpr int kBarPHalf = 6;     // [2] rank 0: P_t keys 0-63 written by the 8 softmax warps of tile t
+constexpr int kBarPFull = 8;     // [2] rank 0: P_t keys 64-127 written (and O_t rescaled)
 constexpr int kBarOStaged = 10;  // [2] O tile staged in smem (128 threads)                       local
 constexpr int kBarDrain = 12;    // [2] rank 0: MMA drain of issuer t at exit
-constexpr int kBarPFree = 14;    // [2] PV_t of a block done        (pair commit to both CTAs)
-constexpr int kBarKVFull = 16;   // [kStages] (rank 0: own TMA + rank 1's forward)
+constexpr int kBarOFinal = 14;   // [2] last PV_t of an item done   (pair commit to both CTAs)
+constexpr int kBarSHi = 16;      // [2] S_t keys 64-127 of a block computed (pair commit to both CTAs)
+constexpr int kBarKVFull = 18;   // [kStages] (rank 0: own TMA + rank 1's forward)
 constexpr int kBarKVEmpty = kBarKVFull + kStages;  // [kStages] released by both tiles' softmax   local
 constexpr int kNumBars = kBarKVEmpty + kStages;
-constexpr uint32_t kTileWarps = 8;  // softmax warps per tile in the pair (arrivals on S free / P full)
+constexpr uint32_t kTileWarps = 8;  // softmax warps per tile in the pair (arrivals on P half / P full)
 
 constexpr int kSmemQ = 0;
 constexpr int kSmemKV = 2 * kQTileBytes;
@@ -131,15 +147,15 @@ constexpr int kSmemUsed = kSmemMisc + 16;
 constexpr int kSmemBytes = kSmemUsed + 1024;  // + slack for 1024-B alignment
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 static_assert(kSmemBar % 8 == 0, "mbarrier alignment");
-static_assert(kKHalfBytes % 1024 == 0 && kStageBytes % 1024 == 0, "128-byte swizzle atoms must stay 1024-B aligned");
+static_assert(kKBoxBytes % 1024 == 0 && kStageBytes % 1024 == 0, "128-byte swizzle atoms must stay 1024-B aligned");
 
 // tcgen05 instruction descriptors, kind::f16 (PTX ISA "Instruction
 // descriptor"): bits 4-5 D format (1 = F32), 7-9 A format (0 = F16),
 // 10-12 B format (0 = F16), 15 A major (0 = K), 16 B major (1 = MN),
 // 17-22 N>>3, 24-28 M>>4.  M = 256: the pair's rows.
-constexpr uint32_t kIdescQK = (1u << 4) | (uint32_t(kBlockN >> 3) << 17) | (uint32_t(256 >> 4) << 24);
+constexpr uint32_t kIdescQK = (1u << 4) | (uint32_t((kBlockN / 2) >> 3) << 17) | (uint32_t(256 >> 4) << 24);
 constexpr uint32_t kIdescPV = (1u << 4) | (1u << 16) | (uint32_t(kHeadDim >> 3) << 17) | (uint32_t(256 >> 4) << 24);
-static_assert(kBlockN % 16 == 0 && kBlockN <= 256, "M=256 needs N a multiple of 16");
+static_assert((kBlockN / 2) % 16 == 0 && kBlockN <= 256, "M=256 needs N a multiple of 16");
 
 // Shared-memory matrix descriptors (PTX ISA "Matrix Descriptor"), 128-byte
 // swizzle, sm_100 version bit.  Low word: start address >> 4 (bits 0-13),
@@ -214,11 +230,11 @@ constexpr uint32_t kFlagCapture = 8u;
 // clock64() at fixed points of its first work item's first kTimelineBlocks
 // key blocks.  Layout: u64 [role][block][event] at byte kTimelineOffset of
 // the workspace; roles 0/1 = softmax tile 0/1 (warp 4t, lane 0), 2 = MMA
-// threads, 3 = TMA thread.  Softmax events: 0 S ready, 1 S loaded, 2 row
-// max / rescale decided, 3 exponentials done, 4 P handed over.  MMA events
-// of tile t's issuer at 4t + {0 iteration start, 1 S_t(j+1) issued, 2
-// PV_t(j) issued, 3 committed}.  TMA events: 0/1 K wait/issue, 2/3 V
-// wait/issue.
+// threads, 3 = TMA thread.  Softmax events: 0 S low ready, 1 keys 0-63
+// loaded, 2 row max / rescale decided, 3 P half handed over, 4 P full handed
+// over.  MMA events of tile t's issuer at 4t + {0 iteration start, 1 "P
+// half" seen, 2 "P full" seen, 3 second window issued}.  TMA events: 0/1 K
+// wait/issue, 2/3 V wait/issue.
 constexpr int kTimelineBlocks = 48;
 constexpr uint32_t kTimelineOffset = 256u + 32u * 1024u;
 
@@ -358,51 +374,52 @@ __device__ void mma_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base,
   const uint32_t ring_lo = desc_lo(sm.kv(0));   // + slot * (kStageBytes >> 4)
   const uint32_t tS = tmem_base + kTmemS + 128u * t;
   const uint32_t tO = tmem_base + kTmemO + 128u * t;
-  const uint32_t tP = tmem_base + kTmemP + 128u * t;
-  uint32_t kv_base = 0;      // ring position of the current item's K_0
-  uint32_t s_issued = 0;     // S products issued (S-free parity)
-  uint32_t pv_issued = 0;    // PV products issued (P-full parity)
+  uint32_t kv_base = 0;   // ring position of the current item's K_0
+  uint32_t p_phase = 0;   // parity of "P half" / "P full" t
   bool ok = true;
 
-  // S_t = Q_t K^T for the block at ring position `pos` (overwrite); waits for
-  // the 8 softmax warps of tile t to have read the previous S_t (the first
-  // wait passes on the fresh barrier).
-  auto issue_s = [&](uint32_t pos) -> bool {
-    if (!w.wait(sm.bar(kBarKVFull + ring_slot(pos)), ring_parity(pos), site | kBarKVFull)) return false;
-    if (!w.wait(sm.bar(kBarSFree + t), (s_issued & 1u) ^ 1u, site | (kBarSFree + t))) return false;
-    ++s_issued;
-    tc_fence_after();
-    mma_pair_ss_k128<uint32_t(kQHalfBytes >> 4), uint32_t(kKHalfBytes >> 4)>(
-        tS, q_lo, ring_lo + ring_slot(pos) * uint32_t(kStageBytes >> 4), kDescHi, kIdescQK);
-    return true;
+  auto kv_ready = [&](uint32_t pos) -> bool {
+    return w.wait(sm.bar(kBarKVFull + ring_slot(pos)), ring_parity(pos), site | kBarKVFull);
   };
-  // O_t (+)= P_t V for the block whose V sits at ring position `pos`.
-  auto issue_o = [&](uint32_t pos, bool first) -> bool {
-    if (!w.wait(sm.bar(kBarKVFull + ring_slot(pos)), ring_parity(pos), site | kBarKVFull)) return false;
-    if (!w.wait(sm.bar(kBarPFull + t), pv_issued & 1u, site | (kBarPFull + t))) return false;
-    ++pv_issued;
-    tc_fence_after();
-    mma_pair_ts_k80(tO, tP, ring_lo + ring_slot(pos) * uint32_t(kStageBytes >> 4), kDescHi, kIdescPV,
-                    first ? 0u : 1u);
-    return true;
+  auto stage_lo = [&](uint32_t pos) -> uint32_t { return ring_lo + ring_slot(pos) * uint32_t(kStageBytes >> 4); };
+  // One half (keys 0-63: h = 0, keys 64-127: h = 1) of S_t = Q_t K^T for
+  // the block whose K sits at ring position `pos`, into S_t columns
+  // [64h, 64h+64); each CTA supplies 32 keys of the half.
+  auto issue_s_half = [&](uint32_t pos, int h) {
+    mma_pair_ss_k128<uint32_t(kQHalfBytes >> 4), uint32_t(kKBoxBytes >> 4)>(
+        tS + 64u * uint32_t(h), q_lo, stage_lo(pos) + uint32_t(h) * uint32_t(kKPartBytes >> 4), kDescHi, kIdescQK);
+    mma_commit_pair_both(sm.bar((h == 0 ? kBarSLo : kBarSHi) + t));
   };
 
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
     const Timeline tl = make_timeline(p, it);
     const uint32_t ip = uint32_t(it) & 1u;
     if (!w.wait(sm.bar(kBarQFull + t), ip, site | (kBarQFull + t))) break;
-    if (!issue_s(kv_base)) break;  // S_t(0)
-    mma_commit_pair_both(sm.bar(kBarSFull + t));
+    if (!kv_ready(kv_base)) break;
+    tc_fence_after();
+    issue_s_half(kv_base, 0);  // S_t(0)
+    issue_s_half(kv_base, 1);
     for (int j = 0; j < n; ++j) {
+      const uint32_t vpos = kv_base + 2u * uint32_t(j) + 1u;
+      const bool more = j + 1 < n;
       tl.mark(2, j, 4 * t + 0);
-      if (j + 1 < n) {
-        if (!issue_s(kv_base + 2u * uint32_t(j + 1))) { ok = false; break; }
-        mma_commit_pair_both(sm.bar(kBarSFull + t));
-      }
+      // Both stages first: after each PV half this thread touches no shared
+      // memory before the S half that reuses its P columns.
+      if (!kv_ready(vpos) || (more && !kv_ready(vpos + 1u))) { ok = false; break; }
+      if (!w.wait(sm.bar(kBarPHalf + t), p_phase, site | (kBarPHalf + t))) { ok = false; break; }
       tl.mark(2, j, 4 * t + 1);
-      if (!issue_o(kv_base + 2u * uint32_t(j) + 1u, j == 0)) { ok = false; break; }
+      tc_fence_after();
+      // "P half": S_t(j) keys 0-63 are read (P sits in the upper columns),
+      // so S_t(j+1) keys 0-63 go first and are ready early.
+      if (more) issue_s_half(vpos + 1u, 0);
+      mma_pair_ts_k64(tO, tS + kTmemPLo, stage_lo(vpos), kDescHi, kIdescPV, j == 0 ? 0u : 1u);
+      if (!w.wait(sm.bar(kBarPFull + t), p_phase, site | (kBarPFull + t))) { ok = false; break; }
+      p_phase ^= 1u;
       tl.mark(2, j, 4 * t + 2);
-      mma_commit_pair_both(sm.bar(kBarPFree + t));
+      tc_fence_after();
+      mma_pair_ts_k64(tO, tS + kTmemPHi, stage_lo(vpos) + 4u * 128u, kDescHi, kIdescPV, 1u);
+      if (more) issue_s_half(vpos + 1u, 1);  // keys 64-127, over both P halves: after both PV halves
+      else mma_commit_pair_both(sm.bar(kBarOFinal + t));
       tl.mark(2, j, 4 * t + 3);
     }
     kv_base += 2u * uint32_t(n);
@@ -476,11 +493,15 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, u
         if (!w.wait(sm.bar(kBarKVEmpty + s), ph ^ 1u, site | (kBarKVEmpty + s))) { ok = false; break; }
         tl.mark(3, j, 2 * which + 1);
         mbar_arrive_expect_tx(sm.bar(kBarKVFull + s), kStageBytes);
-        if (which == 0) {  // keys [j*80 + 40r, +40), all 128 head-dim columns
-          const int krow = j * kBlockN + int(rank) * kPairKeys;
-          tma_load_3d(sm.kv(s), &p.tm_k, sm.bar(kBarKVFull + s), 0, krow, kvh);
-          tma_load_3d(sm.kv(s) + kKHalfBytes, &p.tm_k, sm.bar(kBarKVFull + s), 64, krow, kvh);
-        } else {           // keys [j*80, +80), head-dim columns [64r, +64)
+        if (which == 0) {  // keys [j*128 + 64h + 32r, +32) of each half h, all 128 head-dim columns
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int krow = j * kBlockN + h * (kBlockN / 2) + int(rank) * kKBoxRows;
+            const uint32_t dst = sm.kv(s) + uint32_t(h * kKPartBytes);
+            tma_load_3d(dst, &p.tm_k, sm.bar(kBarKVFull + s), 0, krow, kvh);
+            tma_load_3d(dst + kKBoxBytes, &p.tm_k, sm.bar(kBarKVFull + s), 64, krow, kvh);
+          }
+        } else {           // keys [j*128, +128), head-dim columns [64r, +64)
           tma_load_3d(sm.kv(s), &p.tm_v, sm.bar(kBarKVFull + s), int(rank) * kPairDims, j * kBlockN, kvh);
         }
         issued |= 1u << s;
@@ -549,17 +570,32 @@ __device__ __forceinline__ void exp_keys(const uint32_t* r, uint64_t sl2x2, uint
   }
 }
 
-// Row maximum of the block's 80 scores: 3-input max, four independent chains.
-__device__ __forceinline__ float row_max80(const uint32_t* r) {
+// Row maximum of 64 scores: 3-input max, four independent chains.
+__device__ __forceinline__ float row_max64(const uint32_t* r) {
   float mc0 = -INFINITY, mc1 = -INFINITY, mc2 = -INFINITY, mc3 = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < kBlockN; i += 8) {
+  for (int i = 0; i < 64; i += 8) {
     mc0 = max3(mc0, __uint_as_float(r[i + 0]), __uint_as_float(r[i + 1]));
     mc1 = max3(mc1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
     mc2 = max3(mc2, __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
     mc3 = max3(mc3, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
   }
   return fmaxf(fmaxf(mc0, mc1), fmaxf(mc2, mc3));
+}
+
+// Keys at or beyond `valid` (the last block's key count) get score -inf.
+__device__ __forceinline__ void mask_keys64(uint32_t* r, int first_key, int valid) {
+#pragma unroll
+  for (int i = 0; i < 64; ++i)
+    if (first_key + i >= valid) r[i] = __float_as_uint(-INFINITY);
+}
+
+// Scores of keys [first, first+64) of this thread's row from TMEM.
+__device__ __forceinline__ void load_keys64(uint32_t tS, int first, uint32_t* r, bool tail, int valid) {
+  tmem_ld32(tS + uint32_t(first), r);
+  tmem_ld32(tS + uint32_t(first) + 32u, r + 32);
+  tmem_wait_ld();
+  if (tail) mask_keys64(r, first, valid);
 }
 
 // Softmax of one query tile per warpgroup (warps 0-3: tile 0, 4-7: tile 1),
@@ -574,7 +610,6 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
   const int row = wq * 32 + int(lane);
   const uint32_t lane_off = uint32_t(wq * 32) << 16;
   const uint32_t tS = tmem_base + lane_off + kTmemS + uint32_t(t) * 128;
-  const uint32_t tP = tmem_base + lane_off + kTmemP + uint32_t(t) * 128;
   const uint32_t tO = tmem_base + lane_off + kTmemO + uint32_t(t) * 128;
   const uint32_t sQ = sm.q(t);
   const uint32_t site = (rank << 16) | (warp << 8);
@@ -582,10 +617,10 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
   const uint64_t sl2x2 = f2_pack(sl2, sl2);
   const int n = p.n_kv;
   const bool withhold = (p.flags & kFlagTestWithholdP) != 0 && t == 1;
-  // S-free / P-full live in rank 0; each warp arrives once (lane 0), after
-  // its TMEM reads (tcgen05.wait::ld) or writes (tcgen05.wait::st) have
-  // completed, so rank 1's remote arrival can be relaxed.
-  const uint32_t s_free = rank == 0 ? sm.bar(kBarSFree + t) : map_shared(sm.bar(kBarSFree + t), 0);
+  // P half / P full live in rank 0; each warp arrives once (lane 0), after
+  // its TMEM writes completed (tcgen05.wait::st), so rank 1's remote
+  // arrival can be relaxed.
+  const uint32_t p_half = rank == 0 ? sm.bar(kBarPHalf + t) : map_shared(sm.bar(kBarPHalf + t), 0);
   const uint32_t p_full = rank == 0 ? sm.bar(kBarPFull + t) : map_shared(sm.bar(kBarPFull + t), 0);
   auto arrive_rank0 = [&](uint32_t bar) {
     __syncwarp();
@@ -596,18 +631,11 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
   };
   // One thread per tile returns this tile's use of the K/V ring slots to
   // the CTA's producer (a slot takes one arrival per tile): K of block g
-  // once "S full t" g completed, V of block g once "P free t" g completed.
+  // once "S full t" g completed, V of block g once "S full t" g+1 (or "O
+  // final t") completed.
   const bool releaser = wq == 0 && lane == 0;
   uint32_t g = 0;        // key blocks of this CTA so far (ring positions 2g, 2g+1)
-  uint32_t pv_seen = 0;  // "P free t" completions observed (PV_t products known done)
-  auto pv_done_upto = [&](uint32_t need) -> bool {
-    while (pv_seen < need) {
-      if (!w.wait(sm.bar(kBarPFree + t), pv_seen & 1u, site | (kBarPFree + t))) return false;
-      if (releaser) mbar_arrive(sm.bar(kBarKVEmpty + ring_slot(2u * pv_seen + 1u)));
-      ++pv_seen;
-    }
-    return true;
-  };
+  uint32_t s_phase = 0;  // parity of "S full t"
   bool ok = true;
 
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
@@ -630,25 +658,59 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       cap_idx = (size_t(bh) * size_t(n)) * size_t(p.nq) + size_t(qrow);
     }
     const size_t cap_plane = size_t(p.heads) * size_t(n) * size_t(p.nq);
-    for (int j = 0; j < n; ++j, ++g) {
-      if (!w.wait(sm.bar(kBarSFull + t), g & 1u, site | (kBarSFull + t))) { ok = false; break; }
-      tl.mark(t, j, 0);
-      if (releaser) mbar_arrive(sm.bar(kBarKVEmpty + ring_slot(2u * g)));  // S_t(g) read K_g
-      tc_fence_after();
-      uint32_t r[kBlockN];
-      tmem_ld32(tS + 0, r + 0);
-      tmem_ld32(tS + 32, r + 32);
-      tmem_ld16(tS + 64, r + 64);
-      tmem_wait_ld();
-      tc_fence_before();
-      arrive_rank0(s_free);  // rank 0 may overwrite S_t now
-      tl.mark(t, j, 1);
-      if (j == n - 1 && p.nk_tail < kBlockN) {
+    // O after PV_t(jb) (unnormalised FP32, relative to that block's m):
+    // read the row from TMEM (whole warp), store it.
+    auto capture_o = [&](int jb) {
+      float4* orec = reinterpret_cast<float4*>(p.capture + 4 * cap_plane +
+                                               (cap_idx + size_t(jb) * size_t(p.nq)) * size_t(kHeadDim));
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + 32 * c, o);
+        tmem_wait_ld();
+        if (cap_row) {
 #pragma unroll
-        for (int i = 0; i < kBlockN; ++i)
-          if (i >= p.nk_tail) r[i] = __float_as_uint(-INFINITY);
+          for (int u = 0; u < 8; ++u)
+            orec[8 * c + u] = make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]),
+                                          __uint_as_float(o[4 * u + 2]), __uint_as_float(o[4 * u + 3]));
+        }
       }
-      const float m_blk = row_max80(r) * sl2;
+    };
+
+    for (int j = 0; j < n; ++j, ++g) {
+      // Keys 0-63 ("S low" j; it also means PV_t(j-1) keys 0-63 are done):
+      // load, exponentiate speculatively against the current reference
+      // (after the first block), and reduce their maximum.
+      if (!w.wait(sm.bar(kBarSLo + t), s_phase, site | (kBarSLo + t))) { ok = false; break; }
+      tl.mark(t, j, 0);
+      tc_fence_after();
+      const bool tail = (j == n - 1 && p.nk_tail < kBlockN);
+      uint32_t pk[kBlockN / 2];
+      uint64_t acc0 = 0ull, acc1 = 0ull;  // packed FP32 partial row sums
+      float hsum = 0.f;                   // FP16 variant: sums of FP16 group sums
+      float mx;
+      {
+        uint32_t r[64];
+        load_keys64(tS, 0, r, tail, p.nk_tail);
+        tl.mark(t, j, 1);
+        if (j > 0) exp_keys<kVariant, kPolyPairs, 4>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
+        mx = row_max64(r);
+      }
+      // Keys 64-127 ("S high" j: S_t(j) and PV_t(j-1) complete): load and
+      // reduce (their exponentials follow the check).
+      if (!w.wait(sm.bar(kBarSHi + t), s_phase, site | (kBarSHi + t))) { ok = false; break; }
+      s_phase ^= 1u;
+      if (releaser) {
+        mbar_arrive(sm.bar(kBarKVEmpty + ring_slot(2u * g)));                  // S_t(j) read K_j
+        if (j > 0) mbar_arrive(sm.bar(kBarKVEmpty + ring_slot(2u * g - 1u)));  // PV_t(j-1) read V_(j-1)
+      }
+      tc_fence_after();
+      if constexpr (kCapture) {
+        if (cap_on && j > 0) capture_o(j - 1);
+      }
+      uint32_t r1[64];
+      load_keys64(tS, 64, r1, tail, p.nk_tail);
+      const float m_blk = fmaxf(mx, row_max64(r1)) * sl2;
       float alpha = 1.f;
       bool moved = false;
       if (m_blk > m_ref + kRescaleLog2) {
@@ -658,32 +720,38 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       }
       l *= alpha;
       tl.mark(t, j, 2);
-      // P_t and O_t are in use by PV_t(g-1) until "P free t" g-1.
-      const bool rescale = j > 0 && __any_sync(0xffffffffu, moved);
-      if (rescale) {
-        if (!pv_done_upto(g)) { ok = false; break; }
-        tc_fence_after();
+      if (__any_sync(0xffffffffu, moved)) {
+        // Lazy correction of the running output before any of this block's
+        // P is handed over (PV_t(j-1) is complete: "S high" j covers it;
+        // the P stores' wait below also covers these stores).  Then keys
+        // 0-63 again from S, which is intact until P is written.
+        if (j > 0) {
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + 32 * c, o);
-          tmem_wait_ld();
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + 32 * c, o);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + 32 * c, o);
+          }
+        }
+        uint32_t r[64];
+        load_keys64(tS, 0, r, tail, p.nk_tail);
+        if (moved) {
+          acc0 = 0ull;
+          acc1 = 0ull;
+          hsum = 0.f;
+          exp_keys<kVariant, kPolyPairs, 4>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
         }
       }
-      uint32_t pk[kBlockN / 2];
-      uint64_t acc0 = 0ull, acc1 = 0ull;  // packed FP32 partial row sums
-      float hsum = 0.f;                   // FP16 variant: sums of FP16 group sums
-      exp_keys<kVariant, kPolyPairs, kBlockN / 16>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
+      tmem_st32(tS + kTmemPLo, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      arrive_rank0(p_half);
       tl.mark(t, j, 3);
-      if (!rescale) {
-        if (!pv_done_upto(g)) { ok = false; break; }
-        tc_fence_after();
-      }
-      tmem_st32(tP, pk);
-      tmem_st8(tP + 32, pk + 32);
+      exp_keys<kVariant, kPolyPairs, 4>(r1, sl2x2, f2_pack(-m_ref, -m_ref), pk + 32, acc0, acc1, hsum);
+      tmem_st32(tS + kTmemPHi, pk + 32);
       tmem_wait_st();
       tc_fence_before();
       if (!(withhold && it == 0 && j == 0)) arrive_rank0(p_full);
@@ -693,40 +761,25 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       f2_unpack(acc1, a1, b1);
       const float z = ((a0 + b0) + (a1 + b1)) + hsum;
       l += z;
-      if (kCapture && cap_on) {
-        const size_t idx = cap_idx + size_t(j) * size_t(p.nq);
+      if constexpr (kCapture) {
         if (cap_row) {
-          float* rec = p.capture + idx;
+          float* rec = p.capture + cap_idx + size_t(j) * size_t(p.nq);
           rec[0] = m_ref;
           rec[cap_plane] = l;
           rec[2 * cap_plane] = j == 0 ? 0.f : alpha;
           rec[3 * cap_plane] = z;
         }
-        // O after PV_t(j) (unnormalised FP32, relative to m_ref): wait for
-        // that product, read the row from TMEM (whole warp), store it.
-        if (!pv_done_upto(g + 1)) { ok = false; break; }
-        tc_fence_after();
-        float4* orec = reinterpret_cast<float4*>(p.capture + 4 * cap_plane + idx * size_t(kHeadDim));
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + 32 * c, o);
-          tmem_wait_ld();
-          if (cap_row) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              orec[8 * c + u] = make_float4(__uint_as_float(o[4 * u]), __uint_as_float(o[4 * u + 1]),
-                                            __uint_as_float(o[4 * u + 2]), __uint_as_float(o[4 * u + 3]));
-          }
-        }
-        tc_fence_before();
       }
     }
     if (!ok) break;
 
     // ---- epilogue: O / l -> FP16 -> swizzled smem (this tile's Q buffer) -> TMA store
-    if (!pv_done_upto(g)) { ok = false; break; }  // PV_t of the item's last block done
+    if (!w.wait(sm.bar(kBarOFinal + t), uint32_t(it) & 1u, site | (kBarOFinal + t))) { ok = false; break; }
+    if (releaser) mbar_arrive(sm.bar(kBarKVEmpty + ring_slot(2u * g - 1u)));  // V of the item's last block
     tc_fence_after();
+    if constexpr (kCapture) {
+      if (cap_on) capture_o(n - 1);
+    }
     const float inv_l = 1.f / l;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
@@ -784,16 +837,14 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
     for (int t = 0; t < 2; ++t) {
       mbar_init(sm.bar(kBarQFull + t), fed);
       mbar_init(sm.bar(kBarQEmpty + t), 1);
-      mbar_init(sm.bar(kBarSFree + t), kTileWarps);
+      mbar_init(sm.bar(kBarPHalf + t), kTileWarps);
       mbar_init(sm.bar(kBarPFull + t), kTileWarps);
       mbar_init(sm.bar(kBarOStaged + t), 128);
+      mbar_init(sm.bar(kBarSLo + t), 1);
+      mbar_init(sm.bar(kBarSHi + t), 1);
+      mbar_init(sm.bar(kBarOFinal + t), 1);
+      mbar_init(sm.bar(kBarDrain + t), 1);
     }
-    mbar_init(sm.bar(kBarSFull + 0), 1);
-    mbar_init(sm.bar(kBarSFull + 1), 1);
-    mbar_init(sm.bar(kBarPFree + 0), 1);
-    mbar_init(sm.bar(kBarPFree + 1), 1);
-    mbar_init(sm.bar(kBarDrain + 0), 1);
-    mbar_init(sm.bar(kBarDrain + 1), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(sm.bar(kBarKVFull + s), fed);
       mbar_init(sm.bar(kBarKVEmpty + s), 2);  // one release per tile

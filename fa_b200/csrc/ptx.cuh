@@ -257,10 +257,11 @@ __device__ __forceinline__ void mma_pair_ss_k128(uint32_t d_tmem, uint32_t a_lo,
       : "memory");
 }
 
-// O (+)= P * V for the pair over 80 keys as 5 K=16 steps: A = P from each
+// O (+)= P * V for the pair over 64 keys as 4 K=16 steps: A = P from each
 // CTA's TMEM (8 columns per step), B = V (MN-major, this CTA's 64 head-dim
-// columns; 16 keys = 2 KiB per step).  `first_acc` applies to step 0.
-__device__ __forceinline__ void mma_pair_ts_k80(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
+// columns; 16 keys = 2 KiB per step).  first_acc = 0 overwrites O with the
+// first step.
+__device__ __forceinline__ void mma_pair_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
                                                 uint32_t idesc, uint32_t first_acc) {
   asm volatile(
       "{\n\t"
@@ -276,8 +277,6 @@ __device__ __forceinline__ void mma_pair_ts_k80(uint32_t d_tmem, uint32_t a_tmem
       "add.u32 ta, %1, 16;\n\t add.u32 bl, %2, 256;\n\t mov.b64 db, {bl, %3};\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
       "add.u32 ta, %1, 24;\n\t add.u32 bl, %2, 384;\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
-      "add.u32 ta, %1, 32;\n\t add.u32 bl, %2, 512;\n\t mov.b64 db, {bl, %3};\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
       "}\n" ::"r"(d_tmem),
       "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(first_acc)

@@ -24,7 +24,7 @@ FLAG_TRACE = 1
 FLAG_TEST_WITHHOLD_P = 2
 FLAG_TIMELINE = 4
 FLAG_CAPTURE = 8
-BLOCK_KEYS = 80
+BLOCK_KEYS = 128
 
 DEV_OK = 0
 DEV_TIMEOUT = 1

@@ -102,11 +102,11 @@ extern "C" {
  * The reference's capture holds the same (m, l, alpha, z, O) per packet.
  * Key blocks are B200FA_BLOCK_KEYS keys wide.  Rows of the unit range only;
  * other entries are left untouched.  The buffer must be 16-byte aligned;
- * size: b200fa_capture_bytes() = 528 * B * Hq * ceil(Nk / 80) * Nq.  The
+ * size: b200fa_capture_bytes() = 528 * B * Hq * ceil(Nk / 128) * Nq.  The
  * capture serialises each block's softmax with its P V product: a debug
  * mode, not a fast path. */
 #define B200FA_FLAG_CAPTURE        8u
-#define B200FA_BLOCK_KEYS         80
+#define B200FA_BLOCK_KEYS        128
 
 typedef struct b200fa_options {
     uint32_t struct_size;   /* sizeof(b200fa_options); 16 (no capture fields)
@@ -199,8 +199,9 @@ int64_t b200fa_plan_item(int64_t B, int64_t Hq, int64_t Nq,
                          int64_t unit_begin, int64_t unit_end, int64_t index,
                          int64_t* bh, int64_t* qblock, int64_t* count);
 
-/* Bytes of the B200FA_FLAG_CAPTURE buffer: 16 * B * Hq * ceil(Nk / 80) * Nq
- * (four FP32 planes).  Negative on invalid sizes. */
+/* Bytes of the B200FA_FLAG_CAPTURE buffer:
+ * 528 * B * Hq * ceil(Nk / B200FA_BLOCK_KEYS) * Nq (four scalar FP32 planes
+ * and the 128-float O plane).  Negative on invalid sizes. */
 int64_t b200fa_capture_bytes(int64_t B, int64_t Hq, int64_t Nq, int64_t Nk);
 
 /* Description of the last error on the calling thread ("" if none). */

@@ -115,7 +115,7 @@ def attention_f64(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float | No
 
 
 def online_state_f64(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float | None = None,
-                     block: int = 80, threshold: float = 8.0) -> dict:
+                     block: int = 128, threshold: float = 8.0) -> dict:
     """float64 restatement of the per-block online-softmax state that the
     debug capture records, for small cases.
 

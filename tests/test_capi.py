@@ -129,7 +129,7 @@ def _fwd_ex(flags, capture, capture_bytes):
 def test_capture_size_and_validation_without_gpu():
     # four FP32 planes + the 128-float O plane per (b*Hq+hq, key block, query row)
     need = lib.capture_bytes(1, 2, 300, 1000)
-    assert need == 528 * 2 * 13 * 300
+    assert need == 528 * 2 * -(-1000 // lib.BLOCK_KEYS) * 300
     with pytest.raises(lib.B200FAError):
         lib.capture_bytes(0, 2, 300, 1000)
     assert _fwd_ex(lib.FLAG_CAPTURE, None, need) == -11      # no buffer

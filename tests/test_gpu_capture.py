@@ -29,9 +29,9 @@ from oracle.attention_ref import online_state_f64
 # computes P = 2^x in FP32 (MUFU or a degree-3 polynomial, <= 1e-4
 # relative); the FP16 one rounds x to FP16 and sums FP16 exponentials in
 # groups of eight, and exponentials below 2^-14 are FP16 subnormals (spacing
-# 2^-24): a block far below the running maximum carries up to 80 * 2^-25
+# 2^-24): a block far below the running maximum carries up to 128 * 2^-25
 # absolute error in z.
-TOL = {"fp32": (2e-4, 2e-3, 1e-7), "fp16": (1e-2, 5e-3, 4e-6)}
+TOL = {"fp32": (2e-4, 2e-3, 1e-7), "fp16": (1e-2, 5e-3, 6e-6)}
 
 
 def _inputs(B, Hq, Hkv, Nq, Nk, kscale=1.0, seed=0):
@@ -58,7 +58,9 @@ def test_capture_matches_oracle(variant, shape, kscale):
     assert torch.equal(out, plain)
 
     got = {n: t.cpu().double().numpy() for n, t in Operator.capture_view(cap, q, k).items()}
-    ref = online_state_f64(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy())
+    from fa_b200 import lib
+
+    ref = online_state_f64(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), block=lib.BLOCK_KEYS)
     for n in ("m", "l", "alpha", "z", "o"):
         assert np.isfinite(got[n]).all(), n
     keep = ref["margin"] > 1e-3  # [B, Hq, Nq]

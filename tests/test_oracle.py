@@ -105,8 +105,8 @@ def test_canonical_inputs_match_reference_generator_on_cpu():
             assert [float(x) for x in t[n].flatten()[:4]] == chk[f"{n}_head"]
 
 
-@pytest.mark.parametrize("Nk,kscale", [(80, 1.0), (250, 1.0), (401, 4.0)])
-def test_online_state_recurrence(Nk, kscale):
+@pytest.mark.parametrize("Nk,kscale,block", [(128, 1.0, 128), (250, 1.0, 128), (401, 4.0, 128), (401, 4.0, 80)])
+def test_online_state_recurrence(Nk, kscale, block):
     """The per-block state restatement (what the debug capture is checked
     against) is consistent: l_j = alpha_j l_(j-1) + z_j, alpha_0 = 0, m never
     decreases and moves only past the threshold, the final (m, l) give the
@@ -115,9 +115,9 @@ def test_online_state_recurrence(Nk, kscale):
     q = rng.standard_normal((1, 2, 40, 128)).astype(np.float16)
     k = (rng.standard_normal((1, 1, Nk, 128)) * kscale).astype(np.float16)
     v = rng.standard_normal((1, 1, Nk, 128)).astype(np.float16)
-    st = online_state_f64(q, k, v)
+    st = online_state_f64(q, k, v, block=block)
     m, l, alpha, z = st["m"], st["l"], st["alpha"], st["z"]
-    nb = -(-Nk // 80)
+    nb = -(-Nk // block)
     assert m.shape == (1, 2, nb, 40) and st["o"].shape == (1, 2, nb, 40, 128)
     assert np.all(alpha[:, :, 0] == 0)
     assert np.all((alpha[:, :, 1:] > 0) & (alpha[:, :, 1:] <= 1))
@@ -127,7 +127,7 @@ def test_online_state_recurrence(Nk, kscale):
     assert np.all((alpha[:, :, 1:] == 1) == (dm == 0))
     np.testing.assert_allclose(l[:, :, 0], z[:, :, 0], rtol=0)
     np.testing.assert_allclose(l[:, :, 1:], alpha[:, :, 1:] * l[:, :, :-1] + z[:, :, 1:], rtol=1e-13)
-    assert np.all(z <= 80 * 2.0 ** 8)
+    assert np.all(z <= block * 2.0 ** 8)
     s = (q[0].astype(np.float64) @ k[0, 0].astype(np.float64).T) * (128 ** -0.5 / np.log(2.0))
     lse2 = np.log2(np.exp2(s - s.max(-1, keepdims=True)).sum(-1)) + s.max(-1)
     np.testing.assert_allclose(m[0, :, -1] + np.log2(l[0, :, -1]), lse2, rtol=0, atol=1e-12)
