@@ -1,10 +1,12 @@
 """b200_fa_fp16 -- sm_100a flash-attention forward, FP16 softmax variant.
 
 The B200 counterpart of the reference's CCE FP16 backend
-(backends/cce_fa_nqkq_nz_resident_v13_q768_pool_i4_p128): FP16 exponent
-arguments, FP16 exp2 (two per MUFU operation) and FP16 partial row sums;
-P in FP16 for the PV product; O accumulated in FP32 in tensor memory and
-normalized in FP32 before the FP16 store.
+(backends/cce_fa_nqkq_nz_resident_v13_q768_pool_i4_p128): P rounded to FP16
+and the row sums taken over that FP16 P in FP16 partial sums (groups of 16
+keys, carried over in FP32), so the normalizer sums exactly the values the
+PV product uses; exponentials in FP32 (MUFU and an FMA-pipe polynomial --
+FP16 exponentials are not faster on B200); O accumulated in FP32 in tensor
+memory and normalized in FP32 before the FP16 store.
 
 External-type backend (core/drivers/external.py contract): ``build`` runs the
 hash-keyed nvcc build (CPU-safe, idempotent), ``adapt`` binds the canonical

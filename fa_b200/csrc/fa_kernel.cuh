@@ -531,42 +531,41 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, u
 // Exponentials of 16*kGroups keys (8 pairs per group) of one row:
 // x = s * scale*log2(e) - m with packed FP32 FMAs; of every 8 pairs the last
 // kPoly go through the FMA-pipe polynomial (exp2_poly2) and the rest through
-// MUFU (FP32 ex2, or FP16x2 ex2 in the FP16 variant).  Writes 8*kGroups
-// packed FP16 pairs of P and adds to the running row-sum accumulators.
+// MUFU (FP32 ex2).  Writes 8*kGroups packed FP16 pairs of P and adds the
+// row sum: FP32 variant, the FP32 exponentials into packed FP32 sums (four
+// chains, folded into acc0/acc1); FP16 variant, the FP16 P itself into
+// packed FP16 sums (four chains; at most 16*kGroups <= 64 terms of <= 2^8,
+// far inside FP16 range), carried over to FP32 once per call (hsum).
 template <int kVariant, int kPoly, int kGroups>
 __device__ __forceinline__ void exp_keys(const uint32_t* r, uint64_t sl2x2, uint64_t nmx2, uint32_t* pk,
                                          uint64_t& acc0, uint64_t& acc1, float& hsum) {
+  uint64_t cacc[4] = {0ull, 0ull, 0ull, 0ull};
+  uint32_t hc[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
   for (int g = 0; g < kGroups; ++g) {
-    uint32_t hacc = 0u;
 #pragma unroll
     for (int pp = 0; pp < 8; ++pp) {
       const int i = g * 8 + pp;  // key pair index
       const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sl2x2, nmx2);
+      uint64_t p2;
       if (pp >= 8 - kPoly) {
-        const uint64_t p2 = exp2_poly2(x2);
-        if (pp & 1) acc1 = f2_add(acc1, p2); else acc0 = f2_add(acc0, p2);
-        float a, b;
-        f2_unpack(p2, a, b);
-        pk[i] = pack_h2(a, b);
-      } else if constexpr (kVariant == 1) {
-        float a, b;
-        f2_unpack(x2, a, b);
-        const float ea = ex2_approx(a), eb = ex2_approx(b);
-        const uint64_t p2 = f2_pack(ea, eb);
-        if (pp & 1) acc1 = f2_add(acc1, p2); else acc0 = f2_add(acc0, p2);
-        pk[i] = pack_h2(ea, eb);
+        p2 = exp2_poly2(x2);
       } else {
         float a, b;
         f2_unpack(x2, a, b);
-        const uint32_t e2 = ex2_approx_h2(pack_h2(a, b));
-        pk[i] = e2;
-        hacc = (pp == 0) ? e2 : hadd2(hacc, e2);
+        p2 = f2_pack(ex2_approx(a), ex2_approx(b));
       }
+      float ea, eb;
+      f2_unpack(p2, ea, eb);
+      pk[i] = pack_h2(ea, eb);
+      if constexpr (kVariant == 1) cacc[pp & 3] = f2_add(cacc[pp & 3], p2);
+      else hc[pp & 3] = (g == 0 && pp < 4) ? pk[i] : hadd2(hc[pp & 3], pk[i]);
     }
-    if constexpr (kVariant == 0) {
-      if (kPoly < 8) hsum += h2_sum_f32(hacc);
-    }
+  }
+  if constexpr (kVariant == 0) hsum += h2_sum_f32(hadd2(hadd2(hc[0], hc[1]), hadd2(hc[2], hc[3])));
+  if constexpr (kVariant == 1) {
+    acc0 = f2_add(acc0, f2_add(cacc[0], cacc[2]));
+    acc1 = f2_add(acc1, f2_add(cacc[1], cacc[3]));
   }
 }
 

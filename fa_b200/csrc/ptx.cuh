@@ -360,13 +360,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// Two base-2 exponentials on packed halves.
-__device__ __forceinline__ uint32_t ex2_approx_h2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
-}
-
 // {hi, lo} -> packed f16x2 (lo in bits 0..15), round to nearest even.
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   uint32_t r;

@@ -45,8 +45,8 @@ extern "C" {
 
 /* Variant selector: softmax arithmetic of the two shipped kernels.
  * B200FA_VARIANT_FP16 mirrors the reference CCE FP16 kernel
- *   (backends/cce_fa_nqkq_nz_resident_v13_q768_pool_i4_p128): FP16 exponent
- *   arguments, FP16 exp2 and FP16 partial row sums.
+ *   (backends/cce_fa_nqkq_nz_resident_v13_q768_pool_i4_p128): row sums in
+ *   FP16 partial sums of the FP16 P (FP32 exponentials).
  * B200FA_VARIANT_FP32 mirrors the CCE FP32 kernel
  *   (backends/cce_fa_nk_nz_vector_fp32_v5_sumpack): FP32 softmax throughout.
  * Both keep P in FP16 for the tensor-core PV product and accumulate O in
