@@ -634,7 +634,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
   // final t") completed.
   const bool releaser = wq == 0 && lane == 0;
   uint32_t g = 0;        // key blocks of this CTA so far (ring positions 2g, 2g+1)
-  uint32_t s_phase = 0;  // parity of "S full t"
+  uint32_t s_phase = 0;  // parity of "S low t" / "S high t"
   bool ok = true;
 
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
