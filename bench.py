@@ -21,6 +21,8 @@ Reported:
   e2e         the same metric through the public operator with host buffers:
               per step each rank copies its Q rows and the full K/V from
               pinned host memory, runs the kernel and copies its O rows back
+              (Operator.forward_host: the range is cut in --e2e-chunks pieces
+              whose Q/O copies overlap the other pieces' kernel launches)
   roofline    tensor-bound: achieved TFLOP/s per kernel launch (CUDA events
               around each launch) against the measured bf16 dense peak
   cpu_baseline the oracle's FP32 PyTorch attention on the host cores over a
@@ -61,6 +63,8 @@ def parse_args():
     p.add_argument("--shape", type=str, default="2,12,1,131072",
                    help="B,Hq,Hkv,N (default: the BASELINE metric config)")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--e2e-chunks", type=int, default=4,
+                   help="pieces of the unit range whose copies overlap the kernel in the e2e leg")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=0)
@@ -301,11 +305,10 @@ def main():
         e2e_steps = max(1, min(args.steps, 5))
 
         def e2e_step():
-            qf[r0:r1].copy_(q_host, non_blocking=True)
-            k.copy_(k_host, non_blocking=True)
-            v.copy_(v_host, non_blocking=True)
-            op(q, k, v, out=o, unit_range=(ub, ue))
-            o_host.copy_(o.view(-1, D)[r0:r1], non_blocking=True)
+            # Operator.forward_host: K/V up, then Q up / kernel / O down per
+            # piece of the unit range, the copies overlapped with the kernel.
+            op.forward_host(q_host, k_host, v_host, o_host, q_dev=q, k_dev=k, v_dev=v, o_dev=o,
+                            unit_range=(ub, ue), chunks=args.e2e_chunks)
 
         e2e_step()
         barrier(world)

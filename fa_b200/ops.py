@@ -21,6 +21,7 @@ import math
 import torch
 
 from . import lib
+from .shard import row_range
 
 HEAD_DIM = 128
 BLOCK_M = 128
@@ -47,8 +48,8 @@ def _geometry(q, k, v):
 class Operator:
     """``op(q, k, v) -> O``: non-causal GQA attention forward, FP16 in/out.
 
-    variant: "fp16" (FP16 exp/partial sums, the CCE FP16 kernel's numerics)
-             or "fp32" (FP32 softmax, the CCE FP32 kernel's numerics).
+    variant: "fp16" (row sums over the FP16 P in FP16 partial sums, after the
+             CCE FP16 kernel) or "fp32" (FP32 softmax, the CCE FP32 kernel).
     """
 
     def __init__(self, variant: str = "fp16", *, timeout_us: int = 0, trace: bool = False,
@@ -61,6 +62,7 @@ class Operator:
         self.flags = lib.FLAG_TRACE if trace else 0
         self.max_ctas = int(max_ctas)
         self.workspaces = {}  # device -> uint8 tensor (zeroed once)
+        self._streams = {}    # device -> (upload, download) streams of forward_host
         lib.load()
 
     @property
@@ -103,6 +105,78 @@ class Operator:
                     flags=self.flags | flags | cap_flag, timeout_us=self.timeout_us, max_ctas=self.max_ctas,
                     capture_ptr=cap_ptr, capture_bytes=cap_bytes)
         return out
+
+    def forward_host(self, q_host, k_host, v_host, out_host, *, q_dev, k_dev, v_dev, o_dev,
+                     scale: float | None = None, unit_range: tuple[int, int] | None = None,
+                     chunks: int = 4) -> None:
+        """O = attention(Q, K, V) from pinned host buffers into a pinned host
+        buffer, with the copies overlapped with the kernel.
+
+        K and V go up first; the unit range is then cut into ``chunks``
+        contiguous pieces (whole work items of four query blocks): piece c's
+        Q rows go up on a copy stream while piece c-1 runs, and its O rows
+        come down on a second copy stream while piece c+1 runs.  ``*_dev``
+        are device buffers of the full shapes; ``q_host`` and ``out_host``
+        hold either the full Q/O or only the unit range's rows (flattened to
+        [rows, 128]); only those rows are moved.  Work is enqueued on the
+        current stream, which also waits for the last download: synchronize
+        it to read ``out_host``.
+        """
+        B, Hq, Hkv, Nq, Nk = _geometry(q_dev, k_dev, v_dev)
+        units = num_units(B, Hq, Nq)
+        ub, ue = (0, units) if unit_range is None else unit_range
+        if not 0 <= ub <= ue <= units:
+            raise ValueError(f"unit range [{ub}, {ue}) outside [0, {units})")
+        R0, R1 = row_range(ub, ue, Nq)
+        for name, t, ref in (("q_host", q_host, q_dev), ("k_host", k_host, k_dev), ("v_host", v_host, v_dev),
+                             ("out_host", out_host, o_dev)):
+            rows_only = name in ("q_host", "out_host") and tuple(t.shape) == (R1 - R0, HEAD_DIM)
+            if (t.device.type != "cpu" or not t.is_pinned() or t.dtype != ref.dtype
+                    or not (t.shape == ref.shape or rows_only)):
+                raise ValueError(f"{name} must be a pinned host tensor shaped like its device buffer")
+        dev = q_dev.device
+        cur = torch.cuda.current_stream(dev)
+        s_in, s_out = self._copy_streams(dev)
+        qd, od = q_dev.view(-1, HEAD_DIM), o_dev.view(-1, HEAD_DIM)
+        qh, oh = q_host.view(-1, HEAD_DIM), out_host.view(-1, HEAD_DIM)
+        qo = 0 if q_host.numel() == q_dev.numel() else R0  # host row of flattened row r: r - qo
+        oo = 0 if out_host.numel() == o_dev.numel() else R0
+        # Piece boundaries on whole items (4 units) from the range start; the
+        # first and last pieces are half-sized (only their upload, resp.
+        # download, is not hidden behind a kernel).
+        items = -(-(ue - ub) // 4)
+        n = max(1, min(int(chunks), items))
+        w = [1.0] * n
+        if n >= 3:
+            w[0] = w[-1] = 0.5
+        acc = [0.0]
+        for x in w:
+            acc.append(acc[-1] + x)
+        bounds = [min(ue, ub + 4 * int(round(items * a / acc[-1]))) for a in acc]
+        s_in.wait_stream(cur)  # the device buffers are free once earlier work on `cur` is
+        ev_q = []
+        with torch.cuda.stream(s_in):
+            k_dev.copy_(k_host, non_blocking=True)
+            v_dev.copy_(v_host, non_blocking=True)
+            for c in range(n):
+                r0, r1 = row_range(bounds[c], bounds[c + 1], Nq)
+                qd[r0:r1].copy_(qh[r0 - qo:r1 - qo], non_blocking=True)
+                ev_q.append(s_in.record_event())
+        for c in range(n):
+            cur.wait_event(ev_q[c])
+            self(q_dev, k_dev, v_dev, scale=scale, out=o_dev, unit_range=(bounds[c], bounds[c + 1]))
+            s_out.wait_stream(cur)
+            r0, r1 = row_range(bounds[c], bounds[c + 1], Nq)
+            with torch.cuda.stream(s_out):
+                oh[r0 - oo:r1 - oo].copy_(od[r0:r1], non_blocking=True)
+        cur.wait_stream(s_out)
+
+    def _copy_streams(self, dev):
+        key = ("copy_streams", dev.index)
+        streams = self._streams.get(key)
+        if streams is None:
+            streams = self._streams[key] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        return streams
 
     CAPTURE_LIMIT = 256 << 20  # bytes; the reference restricts its capture the same way
 
@@ -188,3 +262,4 @@ def flops(B: int, Hq: int, Nq: int, Nk: int, D: int = HEAD_DIM) -> int:
 
 def num_units(B: int, Hq: int, Nq: int) -> int:
     return B * Hq * math.ceil(Nq / BLOCK_M)
+

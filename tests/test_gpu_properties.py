@@ -135,3 +135,34 @@ def test_trace_records_cover_the_grid():
     assert sum(r["items"] for r in recs if r["rank"] == 1) == n_items
     assert all(r["t_end_ns"] > r["t_start_ns"] for r in recs)
     assert len({r["smid"] for r in recs}) == len(recs)  # one persistent CTA per SM
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+@pytest.mark.parametrize("shape,world,rank", [((1, 3, 1, 1000), 1, 0), ((2, 4, 2, 700), 3, 1)])
+def test_forward_host_matches_device_path(chunks, shape, world, rank):
+    """The pipelined host-buffer path (pieces of the unit range with their
+    copies overlapped) gives the device path's O bit for bit, and moves only
+    the unit range's rows."""
+    from fa_b200 import shard
+    from fa_b200.ops import Operator
+
+    B, Hq, Hkv, N = shape
+    q, k, v = _inputs(*shape, seed=7)
+    op = Operator("fp16")
+    (ub, ue), (r0, r1) = shard.shard_rows(B, Hq, N, world, rank)
+    ref = op(q, k, v, out=torch.zeros_like(q), unit_range=(ub, ue)).view(-1, 128)[r0:r1]
+    q_host = q.view(-1, 128)[r0:r1].cpu().pin_memory()
+    k_host, v_host = k.cpu().pin_memory(), v.cpu().pin_memory()
+    o_host = torch.full((r1 - r0, 128), float("nan"), dtype=torch.float16).pin_memory()
+    q_dev, k_dev, v_dev = torch.zeros_like(q), torch.zeros_like(k), torch.zeros_like(v)
+    o_dev = torch.full_like(q, float("nan"))
+    op.forward_host(q_host, k_host, v_host, o_host, q_dev=q_dev, k_dev=k_dev, v_dev=v_dev, o_dev=o_dev,
+                    unit_range=(ub, ue), chunks=chunks)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(o_host, ref.cpu())
+    of = o_dev.view(-1, 128)
+    assert torch.isnan(of[:r0]).all() and torch.isnan(of[r1:]).all()
+    with pytest.raises(ValueError):
+        op.forward_host(q_host.clone(), k_host, v_host, o_host, q_dev=q_dev, k_dev=k_dev, v_dev=v_dev,
+                        o_dev=o_dev, unit_range=(ub, ue))  # not pinned
