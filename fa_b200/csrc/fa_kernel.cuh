@@ -175,7 +175,10 @@ __device__ __forceinline__ uint32_t desc_lo(uint32_t saddr) { return ((saddr & 0
 // the exponent field as an integer.  x is clamped at -120 first so the
 // exponent cannot wrap; 2^-120 is 0 in FP16 and negligible in the FP32 row
 // sum, and masked keys (x = -inf) land there too.
-constexpr int kPolyPairs = 2;  // of every 8 key pairs, these go to the polynomial
+// Of every 8 key pairs, these go to the polynomial (measured per variant:
+// the FP32 variant's packed FP32 sums already load the FMA pipe).
+template <int kVariant>
+constexpr int kPolyPairsOf = kVariant == 0 ? 2 : 1;
 constexpr float kExp2C0 = 0.9999280571937561f;
 constexpr float kExp2C1 = 0.6932609677314758f;
 constexpr float kExp2C2 = 0.2426111251115799f;
@@ -692,7 +695,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
         uint32_t r[64];
         load_keys64(tS, 0, r, tail, p.nk_tail);
         tl.mark(t, j, 1);
-        if (j > 0) exp_keys<kVariant, kPolyPairs, 4>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
+        if (j > 0) exp_keys<kVariant, kPolyPairsOf<kVariant>, 4>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
         mx = row_max64(r);
       }
       // Keys 64-127 ("S high" j: S_t(j) and PV_t(j-1) complete): load and
@@ -741,7 +744,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
           acc0 = 0ull;
           acc1 = 0ull;
           hsum = 0.f;
-          exp_keys<kVariant, kPolyPairs, 4>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
+          exp_keys<kVariant, kPolyPairsOf<kVariant>, 4>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
         }
       }
       tmem_st32(tS + kTmemPLo, pk);
@@ -749,7 +752,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       tc_fence_before();
       arrive_rank0(p_half);
       tl.mark(t, j, 3);
-      exp_keys<kVariant, kPolyPairs, 4>(r1, sl2x2, f2_pack(-m_ref, -m_ref), pk + 32, acc0, acc1, hsum);
+      exp_keys<kVariant, kPolyPairsOf<kVariant>, 4>(r1, sl2x2, f2_pack(-m_ref, -m_ref), pk + 32, acc0, acc1, hsum);
       tmem_st32(tS + kTmemPHi, pk + 32);
       tmem_wait_st();
       tc_fence_before();
