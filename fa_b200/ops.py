@@ -21,7 +21,7 @@ import math
 import torch
 
 from . import lib
-from .shard import row_range
+from .shard import pieces, row_range
 
 HEAD_DIM = 128
 BLOCK_M = 128
@@ -141,18 +141,8 @@ class Operator:
         qh, oh = q_host.view(-1, HEAD_DIM), out_host.view(-1, HEAD_DIM)
         qo = 0 if q_host.numel() == q_dev.numel() else R0  # host row of flattened row r: r - qo
         oo = 0 if out_host.numel() == o_dev.numel() else R0
-        # Piece boundaries on whole items (4 units) from the range start; the
-        # first and last pieces are half-sized (only their upload, resp.
-        # download, is not hidden behind a kernel).
-        items = -(-(ue - ub) // 4)
-        n = max(1, min(int(chunks), items))
-        w = [1.0] * n
-        if n >= 3:
-            w[0] = w[-1] = 0.5
-        acc = [0.0]
-        for x in w:
-            acc.append(acc[-1] + x)
-        bounds = [min(ue, ub + 4 * int(round(items * a / acc[-1]))) for a in acc]
+        bounds = pieces(ub, ue, chunks)  # whole items; the end pieces half-sized
+        n = len(bounds) - 1
         s_in.wait_stream(cur)  # the device buffers are free once earlier work on `cur` is
         ev_q = []
         with torch.cuda.stream(s_in):

@@ -44,6 +44,27 @@ def row_range(unit_begin: int, unit_end: int, Nq: int) -> tuple[int, int]:
     return unit_row(unit_begin, Nq), unit_row(unit_end, Nq)
 
 
+def pieces(unit_begin: int, unit_end: int, chunks: int, item_units: int = 4) -> list[int]:
+    """Boundaries of ``chunks`` contiguous pieces of [unit_begin, unit_end)
+    on whole work items (``item_units`` units from the range start), the
+    first and last pieces half-sized when there are three or more: the
+    schedule of ``Operator.forward_host``, whose end pieces' copies are the
+    ones not hidden behind a kernel.  Returns n+1 increasing boundaries
+    from unit_begin to unit_end (n >= 1; pieces may be empty only when the
+    range is)."""
+    if unit_end < unit_begin or chunks < 1 or item_units < 1:
+        raise ValueError(f"bad pieces({unit_begin}, {unit_end}, {chunks})")
+    items = -(-(unit_end - unit_begin) // item_units)
+    n = max(1, min(int(chunks), items))
+    w = [1.0] * n
+    if n >= 3:
+        w[0] = w[-1] = 0.5
+    acc = [0.0]
+    for x in w:
+        acc.append(acc[-1] + x)
+    return [min(unit_end, unit_begin + item_units * int(round(items * a / acc[-1]))) for a in acc]
+
+
 def shard_rows(B: int, Hq: int, Nq: int, world: int, rank: int) -> tuple[tuple[int, int], tuple[int, int]]:
     """(unit range, flattened row range) of ``rank``."""
     ub, ue = partition(num_units(B, Hq, Nq), world, rank)

@@ -119,3 +119,21 @@ def test_lost_rank_ends_collective_with_error():
             p.kill()
     assert results[1] == "left"
     assert results[0].startswith("error")
+
+
+@pytest.mark.parametrize("ub,ue,chunks", [(0, 24576, 4), (0, 24576, 1), (5, 37, 3), (0, 3, 8), (7, 8, 4),
+                                          (0, 0, 4), (100, 1000, 6), (1, 9, 2)])
+def test_host_path_pieces(ub, ue, chunks):
+    """Pieces of forward_host: cover the range in order, cut only on whole
+    items from the range start, end pieces no larger than the middle ones."""
+    from fa_b200.shard import pieces
+
+    b = pieces(ub, ue, chunks)
+    assert b[0] == ub and b[-1] == ue and all(x <= y for x, y in zip(b, b[1:]))
+    assert 1 <= len(b) - 1 <= max(1, chunks)
+    assert all((x - ub) % 4 == 0 for x in b[:-1])
+    sizes = [y - x for x, y in zip(b, b[1:])]
+    if len(sizes) >= 3 and ue - ub >= 16 * chunks:
+        assert max(sizes[0], sizes[-1]) <= min(sizes[1:-1])
+    with pytest.raises(ValueError):
+        pieces(5, 4, 2)
