@@ -206,8 +206,8 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
 
 struct FwdParams {
   CUtensorMap tm_q;  // (128, Nq, B*Hq)  fp16, box (64, 128, 1), 128-B swizzle
-  CUtensorMap tm_k;  // (128, Nk, B*Hkv)       box (64, 40, 1)
-  CUtensorMap tm_v;  // (128, Nk, B*Hkv)       box (64, 80, 1)
+  CUtensorMap tm_k;  // (128, Nk, B*Hkv)       box (64, 32, 1)
+  CUtensorMap tm_v;  // (128, Nk, B*Hkv)       box (64, 128, 1)
   CUtensorMap tm_o;  // (128, Nq, B*Hq)        box (64, 128, 1)
   int32_t Hq, Hkv, group;   // group = Hq / Hkv
   int32_t nqb;              // ceil(Nq / 128)
@@ -633,7 +633,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
   };
   // One thread per tile returns this tile's use of the K/V ring slots to
   // the CTA's producer (a slot takes one arrival per tile): K of block g
-  // once "S full t" g completed, V of block g once "S full t" g+1 (or "O
+  // once "S high t" g completed, V of block g once "S high t" g+1 (or "O
   // final t") completed.
   const bool releaser = wq == 0 && lane == 0;
   uint32_t g = 0;        // key blocks of this CTA so far (ring positions 2g, 2g+1)
