@@ -19,10 +19,11 @@ flush is needed between steps.
 Reported:
   value       whole-job TFLOPS, 4*B*Hq*Nq*Nk*D / step time, inputs resident
   e2e         the same metric through the public operator with host buffers:
-              per step each rank copies its Q rows and the full K/V from
-              pinned host memory, runs the kernel and copies its O rows back
-              (Operator.forward_host: the range is cut in --e2e-chunks pieces
-              whose Q/O copies overlap the other pieces' kernel launches)
+              per step each rank copies its Q rows and the K/V heads its
+              rows use from pinned host memory, runs the kernel and copies
+              its O rows back (Operator.forward_host: the range is cut in
+              --e2e-chunks pieces whose copies overlap the other pieces'
+              kernels); h2d/d2h bytes are the bytes it moved
   roofline    tensor-bound: achieved TFLOP/s per kernel launch (CUDA events
               around each launch) against the measured bf16 dense peak
   cpu_baseline the oracle's FP32 PyTorch attention on the host cores over a
@@ -304,11 +305,14 @@ def main():
         o_host = torch.empty((r1 - r0, D), dtype=torch.float16, pin_memory=True)
         e2e_steps = max(1, min(args.steps, 5))
 
+        moved = [0, 0]
+
         def e2e_step():
-            # Operator.forward_host: K/V up, then Q up / kernel / O down per
-            # piece of the unit range, the copies overlapped with the kernel.
-            op.forward_host(q_host, k_host, v_host, o_host, q_dev=q, k_dev=k, v_dev=v, o_dev=o,
-                            unit_range=(ub, ue), chunks=args.e2e_chunks)
+            # Operator.forward_host: per piece of the unit range, its K/V
+            # heads and Q rows up, the kernel, its O rows down; the copies
+            # overlap the other pieces' kernels.
+            moved[:] = op.forward_host(q_host, k_host, v_host, o_host, q_dev=q, k_dev=k, v_dev=v, o_dev=o,
+                                       unit_range=(ub, ue), chunks=args.e2e_chunks)
 
         e2e_step()
         barrier(world)
@@ -319,8 +323,7 @@ def main():
         b_.record(stream)
         barrier(world)
         e2e_ms = max_over_ranks(a.elapsed_time(b_), world) / e2e_steps
-        h2d_local = (r1 - r0) * D * 2 + k.numel() * 2 + v.numel() * 2
-        d2h_local = (r1 - r0) * D * 2
+        h2d_local, d2h_local = moved  # bytes forward_host moved per step
         if world > 1:
             import torch.distributed as dist
             t = torch.tensor([h2d_local, d2h_local], dtype=torch.float64, device=dev)

@@ -108,19 +108,22 @@ class Operator:
 
     def forward_host(self, q_host, k_host, v_host, out_host, *, q_dev, k_dev, v_dev, o_dev,
                      scale: float | None = None, unit_range: tuple[int, int] | None = None,
-                     chunks: int = 4) -> None:
+                     chunks: int = 4) -> tuple[int, int]:
         """O = attention(Q, K, V) from pinned host buffers into a pinned host
         buffer, with the copies overlapped with the kernel.
 
-        K and V go up first; the unit range is then cut into ``chunks``
-        contiguous pieces (whole work items of four query blocks): piece c's
-        Q rows go up on a copy stream while piece c-1 runs, and its O rows
-        come down on a second copy stream while piece c+1 runs.  ``*_dev``
-        are device buffers of the full shapes; ``q_host`` and ``out_host``
-        hold either the full Q/O or only the unit range's rows (flattened to
-        [rows, 128]); only those rows are moved.  Work is enqueued on the
-        current stream, which also waits for the last download: synchronize
-        it to read ``out_host``.
+        The unit range is cut into ``chunks`` contiguous pieces (whole work
+        items of four query blocks, the end pieces half-sized).  On an
+        upload stream, each piece's K/V heads not yet on the device go up,
+        then its Q rows; the piece's kernel runs on the current stream once
+        they are there, and its O rows come down on a download stream while
+        the next pieces run.  Only the K/V heads the range uses are moved
+        (a range inside one batch needs only that batch's heads).
+        ``*_dev`` are device buffers of the full shapes; ``q_host`` and
+        ``out_host`` hold either the full Q/O or only the unit range's rows
+        (flattened to [rows, 128]).  Work is enqueued on the current stream,
+        which also waits for the last download: synchronize it to read
+        ``out_host``.  Returns the (host-to-device, device-to-host) bytes.
         """
         B, Hq, Hkv, Nq, Nk = _geometry(q_dev, k_dev, v_dev)
         units = num_units(B, Hq, Nq)
@@ -139,18 +142,36 @@ class Operator:
         s_in, s_out = self._copy_streams(dev)
         qd, od = q_dev.view(-1, HEAD_DIM), o_dev.view(-1, HEAD_DIM)
         qh, oh = q_host.view(-1, HEAD_DIM), out_host.view(-1, HEAD_DIM)
+        kd, vd = k_dev.view(B * Hkv, Nk, HEAD_DIM), v_dev.view(B * Hkv, Nk, HEAD_DIM)
+        kh, vh = k_host.view(B * Hkv, Nk, HEAD_DIM), v_host.view(B * Hkv, Nk, HEAD_DIM)
         qo = 0 if q_host.numel() == q_dev.numel() else R0  # host row of flattened row r: r - qo
         oo = 0 if out_host.numel() == o_dev.numel() else R0
-        bounds = pieces(ub, ue, chunks)  # whole items; the end pieces half-sized
+        nqb, group = -(-Nq // BLOCK_M), Hq // Hkv
+
+        def kv_head(u):  # K/V head (b*Hkv + kvh) of unit u
+            bh = u // nqb
+            return (bh // Hq) * Hkv + (bh % Hq) // group
+
+        bounds = pieces(ub, ue, chunks)
         n = len(bounds) - 1
+        h2d = d2h = 0
+        kv_done = None  # K/V heads [first, kv_done) of the range are uploaded
         s_in.wait_stream(cur)  # the device buffers are free once earlier work on `cur` is
         ev_q = []
         with torch.cuda.stream(s_in):
-            k_dev.copy_(k_host, non_blocking=True)
-            v_dev.copy_(v_host, non_blocking=True)
             for c in range(n):
-                r0, r1 = row_range(bounds[c], bounds[c + 1], Nq)
+                a, b = bounds[c], bounds[c + 1]
+                if b > a:
+                    first, last = kv_head(a), kv_head(b - 1) + 1
+                    lo = first if kv_done is None else max(first, kv_done)
+                    if last > lo:
+                        kd[lo:last].copy_(kh[lo:last], non_blocking=True)
+                        vd[lo:last].copy_(vh[lo:last], non_blocking=True)
+                        h2d += 2 * (last - lo) * Nk * HEAD_DIM * 2
+                        kv_done = last
+                r0, r1 = row_range(a, b, Nq)
                 qd[r0:r1].copy_(qh[r0 - qo:r1 - qo], non_blocking=True)
+                h2d += (r1 - r0) * HEAD_DIM * 2
                 ev_q.append(s_in.record_event())
         for c in range(n):
             cur.wait_event(ev_q[c])
@@ -159,7 +180,9 @@ class Operator:
             r0, r1 = row_range(bounds[c], bounds[c + 1], Nq)
             with torch.cuda.stream(s_out):
                 oh[r0 - oo:r1 - oo].copy_(od[r0:r1], non_blocking=True)
+            d2h += (r1 - r0) * HEAD_DIM * 2
         cur.wait_stream(s_out)
+        return h2d, d2h
 
     def _copy_streams(self, dev):
         key = ("copy_streams", dev.index)

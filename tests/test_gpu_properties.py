@@ -157,10 +157,17 @@ def test_forward_host_matches_device_path(chunks, shape, world, rank):
     o_host = torch.full((r1 - r0, 128), float("nan"), dtype=torch.float16).pin_memory()
     q_dev, k_dev, v_dev = torch.zeros_like(q), torch.zeros_like(k), torch.zeros_like(v)
     o_dev = torch.full_like(q, float("nan"))
-    op.forward_host(q_host, k_host, v_host, o_host, q_dev=q_dev, k_dev=k_dev, v_dev=v_dev, o_dev=o_dev,
-                    unit_range=(ub, ue), chunks=chunks)
+    h2d, d2h = op.forward_host(q_host, k_host, v_host, o_host, q_dev=q_dev, k_dev=k_dev, v_dev=v_dev,
+                               o_dev=o_dev, unit_range=(ub, ue), chunks=chunks)
     torch.cuda.current_stream().synchronize()
     assert torch.equal(o_host, ref.cpu())
+    # only the K/V heads of the range's (b, hq) went up (the others stay zero)
+    nqb = -(-N // 128)
+    heads = sorted({(bh // Hq) * Hkv + (bh % Hq) // (Hq // Hkv) for bh in range(ub // nqb, (ue - 1) // nqb + 1)})
+    assert d2h == (r1 - r0) * 256 and h2d == (r1 - r0) * 256 + 2 * len(heads) * N * 256
+    kf = k_dev.view(B * Hkv, N, 128)
+    for kvh in range(B * Hkv):
+        assert bool(kf[kvh].abs().sum() > 0) == (kvh in heads)
     of = o_dev.view(-1, 128)
     assert torch.isnan(of[:r0]).all() and torch.isnan(of[r1:]).all()
     with pytest.raises(ValueError):
