@@ -27,6 +27,13 @@ SHAPES = [
     (1, 8, 2, 1000, 777),
     (2, 8, 2, 384, 1024),
     (1, 12, 1, 2048, 2048),
+    # tails on the 128-key block's parts (32 keys per CTA per 64-key half):
+    # 1 key, exactly one part (32), one half (64), three parts (96)
+    (1, 2, 1, 1, 1),
+    (1, 2, 1, 129, 129),
+    (1, 4, 1, 160, 160),
+    (1, 2, 1, 300, 192),
+    (1, 2, 2, 64, 224),
 ]
 
 
