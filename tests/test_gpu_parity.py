@@ -69,9 +69,9 @@ def test_parity_vs_oracle(variant, shape):
 def test_large_magnitude_inputs(variant, mag):
     """Peaked softmax (scores up to ~|mag^2 * 4|): lazy rescaling is exercised.
 
-    The FP32 variant meets the absolute bar.  The FP16 variant computes
-    exponentials in FP16 (relative precision ~2^-10), so once the softmax is
-    peaked and |O| approaches |V| its error scales with |O|: the bar there is
+    The FP32 variant meets the absolute bar.  The FP16 variant rounds P to
+    FP16 and sums it in FP16 (relative precision 2^-11 a step), so once the
+    softmax is peaked and |O| approaches |V| its error scales with |O|: the bar there is
     2e-3 relative to max(1, max|O|) -- the FP16 variant's precision caveat.
     """
     from fa_b200.ops import Operator
