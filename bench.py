@@ -29,6 +29,11 @@ Reported:
   cpu_baseline the oracle's FP32 PyTorch attention on the host cores over a
               bounded sample (N=1, rank 0 only)
   clocks      nvidia-smi samples taken during the timed region
+  parity      after the timed region, the timed O checked against FP32
+              attention of sampled query rows (first/last rows of every
+              rank's shard, block edges, seeded random rows); with N > 1
+              every rank's rows are first all-gathered to rank 0 over NCCL
+              (the one collective, verification only)
 
 ``--impl reference`` times the reference's CPU path instead (FP32 PyTorch
 attention, the formula of backends/expert_v2/impl_tl.py:701-717, restated in
@@ -67,6 +72,9 @@ def parse_args():
     p.add_argument("--e2e-chunks", type=int, default=4,
                    help="pieces of the unit range whose copies overlap the kernel in the e2e leg")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-verify", action="store_true",
+                   help="skip the post-timing parity check of the timed O (and its NCCL gather)")
+    p.add_argument("--verify-rows", type=int, default=64)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
@@ -185,6 +193,52 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+def verify_rows(q, k, v, o_full, picks):
+    """Checker (outside the timed region): FP32 attention of the sampled
+    (b, hq, row) query rows against the same rows of ``o_full``.  Plain
+    torch FP32 on the GPU with TF32 off, scale 1/sqrt(128): the formula of
+    the reference's ref_flash_attn (backends/expert_v2/impl_tl.py:701-717).
+    Returns {"max_abs", "mean_abs", "rows"}."""
+    import torch
+
+    G = q.shape[1] // k.shape[1]
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref, got = [], []
+        for b, h, r in picks:
+            s = (k[b, h // G].float() @ q[b, h, r].float()) * (q.shape[-1] ** -0.5)
+            p = torch.softmax(s, dim=0)
+            ref.append(p @ v[b, h // G].float())
+            got.append(o_full[b, h, r].float())
+        d = (torch.stack(got) - torch.stack(ref)).abs()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return {"max_abs": float(d.max()), "mean_abs": float(d.mean()), "rows": len(picks)}
+
+
+def sample_rows(B, Hq, N, world, n_rows, seed=7):
+    """Query rows to check: the first and last row of every rank's shard,
+    128-row block edges, and seeded random rows, ``n_rows`` in all."""
+    import torch
+
+    from fa_b200.shard import shard_rows
+
+    picks = []
+    for r in range(world):
+        _, (r0, r1) = shard_rows(B, Hq, N, world, r)
+        for row in (r0, r1 - 1):
+            bh, i = divmod(row, N)
+            picks.append((bh // Hq, bh % Hq, i))
+    picks += [(0, 0, 127), (0, Hq - 1, 128), (B - 1, Hq // 2, N - 1)]
+    g = torch.Generator().manual_seed(seed)
+    while len(picks) < n_rows:
+        row = int(torch.randint(B * Hq * N, (1,), generator=g))
+        bh, i = divmod(row, N)
+        picks.append((bh // Hq, bh % Hq, i))
+    return picks[:max(n_rows, 2 * world)]
+
+
 def run_reference(args, B, Hq, Hkv, N):
     """--impl reference: the reference CPU path (FP32 PyTorch attention) on rank 0."""
     rank = int(os.environ.get("RANK", "0"))
@@ -292,6 +346,22 @@ def main():
     ms_per_step = total_ms / args.steps
     value = flops_case / (ms_per_step * 1e-3) / 1e12
 
+    # Parity of the timed output (outside the timed region).  With N ranks
+    # every rank's rows are all-gathered over NCCL first, so rank 0 checks
+    # rows from every shard.
+    parity = None
+    if not args.no_verify:
+        from fa_b200.shard import gather_output
+
+        o_full = gather_output(o, B, Hq, N, world, rank) if world > 1 else o
+        if rank == 0:
+            parity = verify_rows(q, k, v, o_full, sample_rows(B, Hq, N, world, args.verify_rows))
+            parity["gathered_ranks"] = world
+            parity["bar"] = {"max_abs": 2e-3, "mean_abs": 2e-4}
+            parity["pass"] = parity["max_abs"] <= 2e-3 and parity["mean_abs"] <= 2e-4
+        del o_full
+        barrier(world)
+
     # End to end through the public operator with host buffers.
     e2e = None
     if not args.no_e2e:
@@ -329,9 +399,16 @@ def main():
             t = torch.tensor([h2d_local, d2h_local], dtype=torch.float64, device=dev)
             dist.all_reduce(t)
             h2d_local, d2h_local = int(t[0].item()), int(t[1].item())
+        # The host-buffer result must be the device path's, bit for bit.
+        torch.cuda.synchronize(dev)
+        same = torch.tensor([1.0 if torch.equal(o_host, o.view(-1, D)[r0:r1].cpu()) else 0.0],
+                            dtype=torch.float64, device=dev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(same, op=dist.ReduceOp.MIN)
         e2e = {"value": round(flops_case / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d_local,
-               "d2h_bytes_per_step": d2h_local}
+               "d2h_bytes_per_step": d2h_local, "output_equals_device_path": bool(same.item() == 1.0)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -390,6 +467,7 @@ def main():
         },
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "parity": parity,
         "gpu_launches": args.steps,
         "clocks": clocks,
         "device_status": list(status),

@@ -49,6 +49,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   attention_fwd_body<1, true>(p);
 }
 
+// Test hook (b200fa_test_exp2): the softmax's two exponential forms on an
+// array, pairwise as the softmax evaluates them -- exp2_poly2 (FMA pipe) into
+// `poly`, MUFU ex2.approx into `mufu`.
+__global__ void __launch_bounds__(256) exp2_probe_kernel(const float* x, float* poly, float* mufu, int64_t n) {
+  const int64_t i = 2 * (int64_t(blockIdx.x) * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const bool two = i + 1 < n;
+  const float a = x[i], b = two ? x[i + 1] : x[i];
+  float pa, pb;
+  f2_unpack(exp2_poly2(f2_pack(a, b)), pa, pb);
+  poly[i] = pa;
+  mufu[i] = ex2_approx(a);
+  if (two) {
+    poly[i + 1] = pb;
+    mufu[i + 1] = ex2_approx(b);
+  }
+}
+
 using KernelFn = void (*)(FwdParams);
 
 KernelFn kernel_for(int variant, bool capture) {
@@ -203,6 +221,75 @@ int check_capture(const b200fa_options& o, int64_t B, int64_t Hq, int64_t Nq, in
   return B200FA_OK;
 }
 
+// Argument checks shared by b200fa_fwd_ex and b200fa_fwd_noalloc, in the
+// order both report them: pointers, shape, variant, scale, unit range,
+// alignment.
+int check_args(const void* q, const void* k, const void* v, const void* o, int64_t B, int64_t Hq, int64_t Hkv,
+               int64_t Nq, int64_t Nk, int64_t D, float scale, int32_t variant, int64_t unit_begin,
+               int64_t unit_end) {
+  if (!q || !k || !v || !o) return fail(B200FA_ERR_NULL, "q, k, v and o must be device pointers");
+  int rc = validate_shape(B, Hq, Hkv, Nq, Nk, D);
+  if (rc != B200FA_OK) return rc;
+  if (variant != B200FA_VARIANT_FP16 && variant != B200FA_VARIANT_FP32)
+    return fail(B200FA_ERR_VARIANT, "unknown variant %d", variant);
+  if (!std::isfinite(scale) || !(scale > 0.f)) return fail(B200FA_ERR_SCALE, "scale must be finite and positive");
+  const int64_t units = B * Hq * ceil_div<int64_t>(Nq, kBlockM);
+  if (unit_begin < 0 || unit_end > units || unit_begin > unit_end)
+    return fail(B200FA_ERR_UNIT_RANGE, "unit range [%lld, %lld) outside [0, %lld)", (long long)unit_begin,
+                (long long)unit_end, (long long)units);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(B200FA_ERR_ALIGNMENT, "tensor pointers must be 16-byte aligned");
+  return B200FA_OK;
+}
+
+// Options (NULL = defaults) and the capture buffer check; *items = work items
+// of the unit range (0: nothing to launch).
+int read_call_options(const b200fa_options* opts, int64_t B, int64_t Hq, int64_t Nq, int64_t Nk, int64_t unit_begin,
+                      int64_t unit_end, b200fa_options* o_full, int64_t* items) {
+  int rc = read_options(opts, o_full);
+  if (rc != B200FA_OK) return rc;
+  if ((rc = check_capture(*o_full, B, Hq, Nq, Nk)) != B200FA_OK) return rc;
+  *items = plan_count<int64_t>(ceil_div<int64_t>(Nq, kBlockM), unit_begin, unit_end);
+  return B200FA_OK;
+}
+
+// Tensor maps and kernel parameters of one call; `ws` is the device scratch
+// (status header, trace records, timeline) the kernel writes.
+int fill_params(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq,
+                int64_t Nk, float scale, int64_t unit_begin, int64_t unit_end, int64_t items,
+                const b200fa_options& opts, void* ws, FwdParams* p) {
+  std::memset(p, 0, sizeof(*p));
+  int rc;
+  if ((rc = encode_map(&p->tm_q, q, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p->tm_k, k, Nk, B * Hkv, kKBoxRows)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p->tm_v, v, Nk, B * Hkv, kBlockN)) != B200FA_OK) return rc;
+  if ((rc = encode_map(&p->tm_o, o, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
+  p->Hq = int32_t(Hq);
+  p->Hkv = int32_t(Hkv);
+  p->group = int32_t(Hq / Hkv);
+  p->nqb = int32_t(ceil_div<int64_t>(Nq, kBlockM));
+  p->n_kv = int32_t(ceil_div<int64_t>(Nk, kBlockN));
+  p->nk_tail = int32_t(Nk - int64_t(p->n_kv - 1) * kBlockN);
+  p->unit_begin = int32_t(unit_begin);
+  p->unit_end = int32_t(unit_end);
+  p->num_items = int32_t(items);
+  p->scale_log2 = float(double(scale) * 1.4426950408889634074);
+  p->flags = opts.flags;
+  p->timeout_ns = uint64_t(opts.timeout_us ? opts.timeout_us : 2000000u) * 1000ull;
+  p->ws = static_cast<uint32_t*>(ws);
+  p->capture = (opts.flags & B200FA_FLAG_CAPTURE) ? opts.capture : nullptr;
+  p->heads = int32_t(B * Hq);
+  p->nq = int32_t(Nq);
+  return B200FA_OK;
+}
+
+int launch(int32_t variant, const FwdParams& p, int grid, void* stream, const char* where) {
+  kernel_for(variant, p.capture != nullptr)<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, where);
+  return B200FA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -248,66 +335,27 @@ int b200fa_fwd_ex(const void* q, const void* k, const void* v, void* o, int64_t 
                   int64_t Nq, int64_t Nk, int64_t D, float scale, int32_t variant, int64_t unit_begin,
                   int64_t unit_end, void* workspace, uint64_t ws_bytes, void* stream, const b200fa_options* opts) {
   g_last_error[0] = '\0';
-  if (!q || !k || !v || !o) return fail(B200FA_ERR_NULL, "q, k, v and o must be device pointers");
-  int rc = validate_shape(B, Hq, Hkv, Nq, Nk, D);
+  int rc = check_args(q, k, v, o, B, Hq, Hkv, Nq, Nk, D, scale, variant, unit_begin, unit_end);
   if (rc != B200FA_OK) return rc;
-  if (variant != B200FA_VARIANT_FP16 && variant != B200FA_VARIANT_FP32)
-    return fail(B200FA_ERR_VARIANT, "unknown variant %d", variant);
-  if (!std::isfinite(scale) || !(scale > 0.f)) return fail(B200FA_ERR_SCALE, "scale must be finite and positive");
-  const int64_t units = B * Hq * ceil_div<int64_t>(Nq, kBlockM);
-  if (unit_begin < 0 || unit_end > units || unit_begin > unit_end)
-    return fail(B200FA_ERR_UNIT_RANGE, "unit range [%lld, %lld) outside [0, %lld)", (long long)unit_begin,
-                (long long)unit_end, (long long)units);
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
-    return fail(B200FA_ERR_ALIGNMENT, "tensor pointers must be 16-byte aligned");
   const uint64_t ws_need = uint64_t(B200FA_WS_TIMELINE_OFFSET) + uint64_t(B200FA_WS_TIMELINE_BYTES);
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 || ws_bytes < ws_need)
     return fail(B200FA_ERR_WORKSPACE, "workspace must be 256-byte aligned and at least %llu bytes",
                 (unsigned long long)ws_need);
   b200fa_options o_full;
-  if ((rc = read_options(opts, &o_full)) != B200FA_OK) return rc;
-  opts = &o_full;
-  if ((rc = check_capture(o_full, B, Hq, Nq, Nk)) != B200FA_OK) return rc;
-  const int64_t nqb = ceil_div<int64_t>(Nq, kBlockM);
-  const int64_t items = plan_count<int64_t>(nqb, unit_begin, unit_end);
+  int64_t items = 0;
+  if ((rc = read_call_options(opts, B, Hq, Nq, Nk, unit_begin, unit_end, &o_full, &items)) != B200FA_OK) return rc;
   if (items == 0) return B200FA_OK;  // empty shard: nothing to launch
 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   int pairs = 0;
-  rc = device_setup(dev, &pairs);
-  if (rc != B200FA_OK) return rc;
-
+  if ((rc = device_setup(dev, &pairs)) != B200FA_OK) return rc;
   FwdParams p;
-  std::memset(&p, 0, sizeof(p));
-  if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv, kKBoxRows)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv, kBlockN)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
-  p.Hq = int32_t(Hq);
-  p.Hkv = int32_t(Hkv);
-  p.group = int32_t(Hq / Hkv);
-  p.nqb = int32_t(nqb);
-  p.n_kv = int32_t(ceil_div<int64_t>(Nk, kBlockN));
-  p.nk_tail = int32_t(Nk - int64_t(p.n_kv - 1) * kBlockN);
-  p.unit_begin = int32_t(unit_begin);
-  p.unit_end = int32_t(unit_end);
-  p.num_items = int32_t(items);
-  p.scale_log2 = float(double(scale) * 1.4426950408889634074);
-  p.flags = opts->flags;
-  p.timeout_ns = uint64_t(opts->timeout_us ? opts->timeout_us : 2000000u) * 1000ull;
-  p.ws = static_cast<uint32_t*>(workspace);
-  p.capture = (opts->flags & B200FA_FLAG_CAPTURE) ? opts->capture : nullptr;
-  p.heads = int32_t(B * Hq);
-  p.nq = int32_t(Nq);
-
-  const int grid = grid_ctas(pairs, opts->max_ctas, items);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  kernel_for(variant, p.capture != nullptr)<<<grid, kThreads, kSmemBytes, st>>>(p);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
-  return B200FA_OK;
+  if ((rc = fill_params(q, k, v, o, B, Hq, Hkv, Nq, Nk, scale, unit_begin, unit_end, items, o_full, workspace, &p)) !=
+      B200FA_OK)
+    return rc;
+  return launch(variant, p, grid_ctas(pairs, o_full.max_ctas, items), stream, "kernel launch");
 }
 
 int b200fa_fwd(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t Hq, int64_t Hkv, int64_t Nq,
@@ -346,6 +394,19 @@ int64_t b200fa_capture_bytes(int64_t B, int64_t Hq, int64_t Nq, int64_t Nk) {
 }
 
 const char* b200fa_last_error_string(void) { return g_last_error; }
+
+int b200fa_test_exp2(const float* x, float* poly, float* mufu, int64_t n, void* stream) {
+  g_last_error[0] = '\0';
+  if (!x || !poly || !mufu) return fail(B200FA_ERR_NULL, "x, poly and mufu must be device pointers");
+  if (n < 0 || n > kMax31) return fail(B200FA_ERR_SHAPE, "n must be in [0, 2^31)");
+  if (n == 0) return B200FA_OK;
+  const int64_t pairs = (n + 1) / 2;
+  const int blocks = int((pairs + 255) / 256);
+  exp2_probe_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, poly, mufu, n);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "exp2 test kernel launch");
+  return B200FA_OK;
+}
 
 const char* b200fa_version(void) { return "b200fa 0.1 sm_100a"; }
 
@@ -388,22 +449,16 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
                                   int64_t unit_begin, int64_t unit_end, void* stream, const b200fa_options* opts,
                                   void** scratch_out) {
   g_last_error[0] = '\0';
-  if (!q || !k || !v || !o) return fail(B200FA_ERR_NULL, "q, k, v and o must be device pointers");
-  int rc = validate_shape(B, Hq, Hkv, Nq, Nk, D);
+  int rc = check_args(q, k, v, o, B, Hq, Hkv, Nq, Nk, D, scale, variant, unit_begin, unit_end);
   if (rc != B200FA_OK) return rc;
-  if (variant != B200FA_VARIANT_FP16 && variant != B200FA_VARIANT_FP32)
-    return fail(B200FA_ERR_VARIANT, "unknown variant %d", variant);
-  if (!std::isfinite(scale) || !(scale > 0.f)) return fail(B200FA_ERR_SCALE, "scale must be finite and positive");
-  const int64_t units = B * Hq * ceil_div<int64_t>(Nq, kBlockM);
-  if (unit_begin < 0 || unit_end > units || unit_begin > unit_end)
-    return fail(B200FA_ERR_UNIT_RANGE, "unit range [%lld, %lld) outside [0, %lld)", (long long)unit_begin,
-                (long long)unit_end, (long long)units);
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
-    return fail(B200FA_ERR_ALIGNMENT, "tensor pointers must be 16-byte aligned");
   b200fa_options o_full;
-  if ((rc = read_options(opts, &o_full)) != B200FA_OK) return rc;
-  opts = &o_full;
-  if ((rc = check_capture(o_full, B, Hq, Nq, Nk)) != B200FA_OK) return rc;
+  int64_t items = 0;
+  if ((rc = read_call_options(opts, B, Hq, Nq, Nk, unit_begin, unit_end, &o_full, &items)) != B200FA_OK) return rc;
+  if (o_full.flags & B200FA_FLAG_TIMELINE)
+    return fail(B200FA_ERR_WORKSPACE,
+                "b200fa_fwd_noalloc does not support B200FA_FLAG_TIMELINE: the timeline needs %u bytes of scratch "
+                "and the static scratch holds %u; use b200fa_fwd_ex with a workspace",
+                unsigned(B200FA_WS_TIMELINE_BYTES), unsigned(B200FA_NOALLOC_SCRATCH_BYTES));
 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -414,14 +469,17 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
   if ((rc = noalloc_scratch(dev, &scratch)) != B200FA_OK) return rc;
   if (scratch_out) *scratch_out = scratch;
 
-  const int64_t nqb = ceil_div<int64_t>(Nq, kBlockM);
-  const int64_t items = plan_count<int64_t>(nqb, unit_begin, unit_end);
-  if (items == 0) return B200FA_OK;
-  const int grid = grid_ctas(pairs, opts->max_ctas, items);
-  const uint64_t need = (opts->flags & B200FA_FLAG_TIMELINE)
-                            ? uint64_t(B200FA_WS_TIMELINE_OFFSET) + B200FA_WS_TIMELINE_BYTES
-                            : uint64_t(B200FA_WS_HEADER_BYTES) +
-                                  ((opts->flags & B200FA_FLAG_TRACE) ? uint64_t(B200FA_WS_TRACE_BYTES) * uint64_t(grid) : 0u);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (items == 0) {
+    // Nothing to launch; the status read through scratch_out must still
+    // describe this call, not an earlier one.
+    e = cudaMemsetAsync(scratch, 0, B200FA_WS_HEADER_BYTES, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(noalloc status header)");
+    return B200FA_OK;
+  }
+  const int grid = grid_ctas(pairs, o_full.max_ctas, items);
+  const uint64_t need = uint64_t(B200FA_WS_HEADER_BYTES) +
+                        ((o_full.flags & B200FA_FLAG_TRACE) ? uint64_t(B200FA_WS_TRACE_BYTES) * uint64_t(grid) : 0u);
   if (need > B200FA_NOALLOC_SCRATCH_BYTES)
     return fail(B200FA_ERR_WORKSPACE,
                 "b200fa_fwd_noalloc: this call needs %llu bytes of scratch (trace records for %d CTAs) but the "
@@ -430,35 +488,12 @@ extern "C" int b200fa_fwd_noalloc(const void* q, const void* k, const void* v, v
                 (unsigned)B200FA_NOALLOC_TRACE_CTAS, (unsigned)B200FA_NOALLOC_TRACE_CTAS);
 
   FwdParams p;
-  std::memset(&p, 0, sizeof(p));
-  if ((rc = encode_map(&p.tm_q, q, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_k, k, Nk, B * Hkv, kKBoxRows)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_v, v, Nk, B * Hkv, kBlockN)) != B200FA_OK) return rc;
-  if ((rc = encode_map(&p.tm_o, o, Nq, B * Hq, kBlockM)) != B200FA_OK) return rc;
-  p.Hq = int32_t(Hq);
-  p.Hkv = int32_t(Hkv);
-  p.group = int32_t(Hq / Hkv);
-  p.nqb = int32_t(nqb);
-  p.n_kv = int32_t(ceil_div<int64_t>(Nk, kBlockN));
-  p.nk_tail = int32_t(Nk - int64_t(p.n_kv - 1) * kBlockN);
-  p.unit_begin = int32_t(unit_begin);
-  p.unit_end = int32_t(unit_end);
-  p.num_items = int32_t(items);
-  p.scale_log2 = float(double(scale) * 1.4426950408889634074);
-  p.flags = opts->flags;
-  p.timeout_ns = uint64_t(opts->timeout_us ? opts->timeout_us : 2000000u) * 1000ull;
-  p.ws = static_cast<uint32_t*>(scratch);
-  p.capture = (opts->flags & B200FA_FLAG_CAPTURE) ? opts->capture : nullptr;
-  p.heads = int32_t(B * Hq);
-  p.nq = int32_t(Nq);
-
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = fill_params(q, k, v, o, B, Hq, Hkv, Nq, Nk, scale, unit_begin, unit_end, items, o_full, scratch, &p)) !=
+      B200FA_OK)
+    return rc;
   // The array keeps the previous call's contents: the status header must start
   // at zero for this call.  Trace records are rewritten by every CTA that runs.
   e = cudaMemsetAsync(scratch, 0, B200FA_WS_HEADER_BYTES, st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(noalloc status header)");
-  kernel_for(variant, p.capture != nullptr)<<<grid, kThreads, kSmemBytes, st>>>(p);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "kernel launch (noalloc)");
-  return B200FA_OK;
+  return launch(variant, p, grid, stream, "kernel launch (noalloc)");
 }

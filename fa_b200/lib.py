@@ -64,6 +64,7 @@ SIGNATURES = {
     "b200fa_capture_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "b200fa_last_error_string": (C.c_char_p, []),
     "b200fa_version": (C.c_char_p, []),
+    "b200fa_test_exp2": (C.c_int, [_p, _p, _p, _i64, _p]),
     "b200fa_fwd_noalloc": (C.c_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i32,
                                      _i64, _i64, _p, C.POINTER(Options), C.POINTER(_p)]),
 }

@@ -210,6 +210,16 @@ const char* b200fa_last_error_string(void);
 /* Library version string. */
 const char* b200fa_version(void);
 
+/* Test hook, no counterpart in the reference: evaluates the softmax's two
+ * exponential forms elementwise on n device floats, asynchronously on
+ * `stream` -- poly[i] = the FMA-pipe 2^x the kernels use for part of every
+ * row (Cody-Waite split, degree-3 minimax polynomial, input clamped at -120),
+ * mufu[i] = the MUFU ex2.approx.ftz form they use for the rest.  Lets a test
+ * check the compiled device function against exp2 over the softmax's input
+ * range.  0, B200FA_ERR_NULL, B200FA_ERR_SHAPE (n < 0 or >= 2^31) or a CUDA
+ * error code. */
+int b200fa_test_exp2(const float* x, float* poly, float* mufu, int64_t n, void* stream);
+
 /* Allocation-free forward.  This entry point has no counterpart in the
  * reference; it exists for callers that cannot hand the library a
  * workspace: a C or FFI host with no device allocator of its own, a runtime
@@ -232,7 +242,10 @@ const char* b200fa_version(void);
  *     (B200FA_FLAG_TRACE) with a persistent grid of more than
  *     B200FA_NOALLOC_TRACE_CTAS CTAs -- is rejected with
  *     B200FA_ERR_WORKSPACE before anything is launched; cap the grid with
- *     opts->max_ctas or trace less.
+ *     opts->max_ctas or trace less.  B200FA_FLAG_TIMELINE is not supported
+ *     here (its area alone exceeds the array) and is rejected the same way.
+ *   - A call with an empty unit range launches nothing but still clears the
+ *     status header, so a status read afterwards describes this call.
  *   - scratch_out (may be NULL) receives the device address of this
  *     device's scratch, for b200fa_read_status / b200fa_reset_status. */
 #define B200FA_NOALLOC_TRACE_CTAS 128u

@@ -88,11 +88,16 @@ def attention_rows_fp32(q, k, v, rows, scale: float | None = None) -> torch.Tens
     G = q.shape[1] // k.shape[1]
     scale = D ** -0.5 if scale is None else scale
     out = torch.empty((rows.shape[0], D), dtype=torch.float32, device=q.device)
-    for i, (b, h, r) in enumerate(rows.tolist()):
-        kf = k[b, h // G].float()
-        s = (q[b, h, r].float() @ kf.T) * scale
-        p = torch.softmax(s, dim=-1)
-        out[i] = p @ v[b, h // G].float()
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for i, (b, h, r) in enumerate(rows.tolist()):
+            kf = k[b, h // G].float()
+            s = (q[b, h, r].float() @ kf.T) * scale
+            p = torch.softmax(s, dim=-1)
+            out[i] = p @ v[b, h // G].float()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev_tf32
     return out
 
 

@@ -1,9 +1,9 @@
 """Generate the golden vectors that pin the oracle to the reference's own code.
 
-Run in the build container, where the reference checkout is readable
-(default /root/reference, or $FA_REFERENCE):
+Run where a checkout of the reference (platelett/fa) is readable, giving
+its root directory (or setting $FA_REFERENCE):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference checkout>
 
 It executes three pieces of the reference and records their results:
 
@@ -38,7 +38,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("FA_REFERENCE", "/root/reference"))
+REF = None  # the reference checkout; set by main() from argv[1] or $FA_REFERENCE
 
 # (B, Hq, Hkv, Nq, Nk, seed, input scale): small cases covering GQA groupings,
 # MHA, query/key tails (N % 128 != 0), Nq != Nk, a single key block and
@@ -134,7 +134,15 @@ def make_cases():
     return ref_cases, extra, checks
 
 
-def main():
+def main(argv=None):
+    global REF
+    argv = sys.argv[1:] if argv is None else argv
+    root = argv[0] if argv else os.environ.get("FA_REFERENCE")
+    if not root:
+        raise SystemExit("usage: make_golden.py <reference checkout>  (or set FA_REFERENCE)")
+    REF = Path(root)
+    if not (REF / "problem" / "cases.py").is_file():
+        raise SystemExit(f"{REF} is not a checkout of the reference (no problem/cases.py)")
     meta, ref_lines = make_vectors()
     ref_cases, extra, canon_checks = make_cases()
     (HERE / "cases.json").write_text(json.dumps({

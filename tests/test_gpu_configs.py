@@ -1,0 +1,88 @@
+"""GPU parity at the BASELINE configurations, against the FP32 oracle run on
+the GPU (TF32 off) on the same seeded canonical inputs.
+
+* C2 (4,32,8,8192) and C3 (1,12,1,32768): every element of O.
+* C4 (2,12,1,65536) and C5 (2,12,1,131072): two whole heads each -- the
+  first head of the first batch and the last head of the last batch, i.e.
+  the first and the last work units of the grid -- plus sampled rows of
+  every head.
+* C1 (1,12,1,2048) runs in full in tests/test_gpu_parity.py.
+
+The cases are the reference's own (problem/cases.py:35-39) plus the two
+configurations BASELINE adds; inputs follow problem/canonical.py:18-28
+(seed 0, q then k then v, N(0,1) FP16) on the GPU's RNG stream.  Bar: max-abs
+<= 2e-3 and mean-abs <= 2e-4 on O, both variants.
+"""
+
+import pytest
+import torch
+
+from oracle.attention_ref import attention_fp32, attention_rows_fp32, errors
+
+MAX_ABS = 2e-3
+MEAN_ABS = 2e-4
+
+CONFIGS = {
+    "C2": (4, 32, 8, 8192),
+    "C3": (1, 12, 1, 32768),
+    "C4": (2, 12, 1, 65536),
+    "C5": (2, 12, 1, 131072),
+}
+
+
+def _canonical(B, Hq, Hkv, N, seed=0):
+    from fa_b200.problem.canonical import build_canonical
+    from fa_b200.problem.cases import Case
+
+    t = build_canonical(Case(batch=B, seq_len=N, heads_q=Hq, heads_kv=Hkv), seed=seed, device="cuda")
+    return t["q"], t["k"], t["v"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("variant", ["fp16", "fp32"])
+@pytest.mark.parametrize("name", ["C2", "C3"])
+def test_whole_output_matches_oracle(variant, name):
+    from fa_b200.ops import Operator
+
+    q, k, v = _canonical(*CONFIGS[name])
+    op = Operator(variant)
+    out = op(q, k, v)
+    torch.cuda.synchronize()
+    assert op.status(q.device)[0] == 0
+    ref = attention_fp32(q, k, v)
+    assert torch.isfinite(out).all()
+    mx, mean = errors(out, ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (name, variant, mx, mean)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("variant", ["fp16", "fp32"])
+@pytest.mark.parametrize("name", ["C4", "C5"])
+def test_whole_heads_and_sampled_rows_match_oracle(variant, name):
+    from fa_b200.ops import Operator
+
+    B, Hq, Hkv, N = CONFIGS[name]
+    G = Hq // Hkv
+    q, k, v = _canonical(B, Hq, Hkv, N)
+    op = Operator(variant)
+    out = op(q, k, v)
+    torch.cuda.synchronize()
+    assert op.status(q.device)[0] == 0
+    assert torch.isfinite(out).all()
+    for b, h in ((0, 0), (B - 1, Hq - 1)):
+        kv = h // G
+        ref = attention_fp32(q[b:b + 1, h:h + 1], k[b:b + 1, kv:kv + 1], v[b:b + 1, kv:kv + 1])
+        mx, mean = errors(out[b:b + 1, h:h + 1], ref)
+        assert mx <= MAX_ABS and mean <= MEAN_ABS, (name, variant, (b, h), mx, mean)
+    # Four rows of every (b, hq): first, last, a block edge, one seeded row.
+    gen = torch.Generator().manual_seed(3)
+    picks = []
+    for b in range(B):
+        for h in range(Hq):
+            picks += [[b, h, 0], [b, h, N - 1], [b, h, 128 * int(torch.randint(N // 128, (1,), generator=gen))],
+                      [b, h, int(torch.randint(N, (1,), generator=gen))]]
+    rows = torch.tensor(picks)
+    ref = attention_rows_fp32(q, k, v, rows.to(q.device))
+    got = torch.stack([out[b, h, r] for b, h, r in picks]).float()
+    mx, mean = errors(got, ref)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (name, variant, "rows", mx, mean)
