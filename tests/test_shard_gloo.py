@@ -51,7 +51,9 @@ def _worker(rank, world, port, shape, result_q):
         if len(rows):
             flat[r0:r1] = attention_rows_fp32(q, k, v, rows)
         full = shard.gather_output(out, B, Hq, N, world, rank)
-        result_q.put((rank, ub, ue, full if rank == 0 else None))
+        # A numpy array is pickled by value: a tensor would be shared through a
+        # file descriptor that dies with this process if it exits first.
+        result_q.put((rank, ub, ue, full.numpy() if rank == 0 else None))
     finally:
         dist.destroy_process_group()
 
@@ -73,7 +75,7 @@ def test_sharded_oracle_equals_unsharded(world, shape):
     results.sort()
     spans = [(ub, ue) for _, ub, ue, _ in results]
     assert spans[0][0] == 0 and all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
-    full = results[0][3]
+    full = torch.from_numpy(results[0][3])
     ref = attention_fp32(*_inputs(*shape))
     assert not torch.isnan(full).any()
     assert torch.allclose(full, ref, atol=1e-6, rtol=0)
