@@ -7,81 +7,74 @@
 //
 // Work decomposition.  A work unit is one 128-row query block of one (b, hq),
 // linearised ((b*Hq)+hq)*ceil(Nq/128)+qb (cce_task.h:28-35 order).  A work
-// item is up to four consecutive units of the same head (512 query rows)
-// that share every K/V block.  Items are dealt round-robin to a persistent
-// grid of CTA pairs (clusters of two CTAs on the two SMs of a TPC), one pair
-// per TPC.
+// item is two consecutive units of the same head, one per CTA of a pair,
+// sharing every K/V block.  Items are dealt round-robin to a persistent grid
+// of CTA pairs (clusters of two CTAs on the two SMs of a TPC), one pair per
+// TPC.
 //
 // The pair.  Both tensor-core products run as pair MMAs (tcgen05
-// cta_group::2, M = 256) issued by rank 0: each CTA holds 128 query rows of
-// a tile, and the B operand is split between the two shared memories --
-// rank r holds keys [64r, 64r+64) of every 128-key K block (S = Q K^T) and
-// head-dim columns [64r, 64r+64) of every V block (O = P V).  Per SM and
-// K=16 step the QK product then reads 4 KiB of Q and 2 KiB of K from shared
-// memory (48 cycles at 128 B/clk against 64 cycles of tensor work), and each
-// SM loads only half of every K/V block.
+// cta_group::2, M = 256) issued by rank 0: each CTA holds its unit's 128
+// query rows, and the B operand is split between the two shared memories --
+// rank r holds keys [64r, 64r+64) of every 128-key K block (S = Q K^T, one
+// N = 128 product per block) and head-dim columns [64r, 64r+64) of every V
+// block (O = P V).  Per SM and K=16 step the S product reads 4 KiB of Q and
+// 2 KiB of K from shared memory (48 cycles at 128 B/clk against 64 of tensor
+// work), and each SM loads only half of every K/V block.
 //
 // CTA roles (384 threads = 3 warpgroups), the same in both CTAs:
-//   warps 0-3   softmax, query tile 0 (TMEM lanes = rows)
-//   warps 4-7   softmax, query tile 1
-//   warp  8/10  rank 0: MMA issuer of tile 0 / tile 1 (one thread each)
+//   warps 0-3   softmax group 0: the item's even key blocks (TMEM lanes = rows)
+//   warps 4-7   softmax group 1: the odd key blocks
+//   warp  8     rank 0: the S issuer (one thread): every S = Q K^T product
 //   warp  9     TMA producer (one thread): this CTA's Q tiles and K/V halves
+//   warp  10    rank 0: the PV issuer (one thread): every O += P V product
 //   warp  11    rank 1: forwards its TMA completions to rank 0's barriers
-// Unit u = 2t + r of an item is tile t of rank r.
 //
-// One issuer thread per tile: a thread that has tcgen05.mma in flight
-// stalls on its next shared-memory access (an mbarrier probe included)
-// until those MMAs drain, so a single issuer that waits between products
-// leaves the tensor pipe idle.  With one issuer per tile, one tile's
-// products keep the pipe busy while the other tile's issuer waits.
+// Schedule.  The CTA counts its key blocks over all its items; block g has
+// its scores in S buffer g % 2 and its P in P buffer g % 2 (both in tensor
+// memory).  The S issuer writes S of block g once the softmax has read the
+// scores of block g - 2 from that buffer ("S free"), so scores run up to two
+// blocks ahead of the softmax; the PV issuer runs O += P V for block g once
+// its P is written ("P full") and then reports the P buffer free and O up
+// to date ("PV done").  Each kind of product has its own issuing thread: a
+// single thread whose stream alternates S and PV products feeds the tensor
+// pipe far below its rate (measured on B200: ~100 cycles per N = 128 pair
+// product instead of ~65); two threads with one kind each keep it busy.
+// The two softmax groups take alternate blocks, each with two block periods
+// for its block; both run at once on every SM sub-partition, so each hides
+// the other's latencies.  K and V have separate rings: a K stage is free
+// once S of its block completed, a V stage once PV did.  Rank 1's TMA
+// completions reach rank 0 through its warp 11, which waits for each local
+// stage and arrives on rank 0's barrier: no copy ever signals the other CTA.
 //
-// Tensor memory, per tile t (same columns in both CTAs):
-//   S_t [128t, 128t+128)     FP32 scores of the current 128-key block, as
-//                            two halves: keys 0-63 in columns [0,64), keys
-//                            64-127 in [64,128).  Once the softmax has read
-//                            them, P_t (FP16 pairs) takes columns [96,128)
-//                            (keys 0-63) and [64,96) (keys 64-127)
-//   O_t [256+128t, +128)     FP32 output accumulator
+// Tensor memory (same columns in both CTAs):
+//   O   [0, 128)             FP32 output accumulator
+//   P_b [128 + 64b, +64)     FP16 P of a block (pairs), b = 0, 1
+//   S_b [256 + 128b, +128)   FP32 scores of a 128-key block (key c in column c)
 //
 // Shared memory (1024-B aligned, 128-byte swizzle as the TMA writes it):
-//   Q0, Q1 (2 x 32 KiB: two 64-column halves of 128 rows; each also stages
-//   its tile's FP16 output for the TMA store), a ring of kStages 16 KiB
-//   stages holding this CTA's part of K_j (32 keys of each S half, as two
-//   64-column boxes of 32 rows per half) and of V_j (one box of 128 rows x
-//   64 columns) alternately, mbarriers.
+//   two Q tiles (32 KiB each: two 64-column halves of 128 rows; item i uses
+//   tile i % 2, so the next item's Q lands while this one runs, and the tile
+//   stages the item's FP16 output for the TMA store), a K ring and a V ring
+//   of kRing stages each (16 KiB: this CTA's 64 keys of a block, as two
+//   64-column boxes, / this CTA's 64 head-dim columns of the block's 128
+//   keys), the softmax groups' exchange area, mbarriers.
 //
-// Per key block j the issuer of tile t works in two windows.  After "P
-// half" j (all 8 softmax warps of the tile, 4 per CTA, have read S_t(j) and
-// written P_t(j) keys 0-63): S_t(j+1) keys 0-63 ("S low" j+1, its columns
-// hold no P), then PV over keys 0-63.  After "P full" j (keys 64-127
-// written): PV over keys 64-127, then S_t(j+1) keys 64-127 ("S high" j+1)
-// over the columns both PV halves read -- one thread issues them, and the
-// tensor pipe executes its products in order.  So S_t(j+1) keys 0-63 are
-// computed while the softmax still works on block j, and the ordering gives
-// the softmax its guarantees without further waits: "S high" j+1 means the
-// PV of block j is complete, so O_t may be rescaled and P_t(j+1) written.
-// Splitting S costs shared-memory bandwidth (an N = 64 half reads Q once
-// per 32 tensor cycles: 40 cycles at 128 B/clk) and buys S(j+1) keys 0-63
-// off the softmax's path.  The softmax releases its use of the K/V ring
-// slots locally (K_j once "S high" j, V_j once "S high" j+1 or, for the
-// item's last block, "O final"); a slot is refilled after both tiles
-// released it.  Rank 1's TMA completions reach rank 0 through its warp 11,
-// which waits for each local stage and arrives on rank 0's barrier: no copy
-// ever signals the other CTA.
-//
-// Online softmax (per query row, one thread per row): running reference
-// maximum m (log2 domain), running sum l.  The reference moves only when a
-// block's maximum exceeds it by more than kRescaleLog2 (lazy rescaling), so
-// P <= 2^kRescaleLog2 and O/l is exact at the end whatever the reference.
-// When it moves, the warp rescales its 32 rows of O in TMEM.  After a
-// tile's first block the exponentials of keys 0-63 are computed against the
-// current reference while keys 64-127 are loaded and reduced, and redone in
-// the rare block where the reference moves.
+// Online softmax (per query row, one thread per row in each group): the
+// reference maximum m (log2 domain) moves only when a block's maximum
+// exceeds it by more than kRescaleLog2 (lazy rescaling), so P <=
+// 2^kRescaleLog2 and O/l is exact at the end whatever the reference.  The
+// reference after block g is passed to the other group through shared memory
+// ("ref g"); the group that moves it rescales the row's O in TMEM (after
+// PV of block g-1 completed) before its P is handed over.  Each group keeps
+// its own partial row sum, relative to the reference of its last block; the
+// two are brought to the final reference and added at the end of the item.
 //
 // Every wait is bounded (global timer); on expiry the kernel records
 // B200FA_DEV_TIMEOUT in the workspace, raises the abort flag of both CTAs,
 // every role leaves its loop, in-flight copies and MMAs are drained with a
-// second bound, TMEM is freed and the kernel returns.
+// second bound, TMEM is freed and the kernel returns.  The checking build
+// (B200FA_DEBUG) also verifies coordinates, indices and layout before use
+// and the roles' block counts at exit (B200FA_DEV_BOUNDS / _PHASE).
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -89,61 +82,65 @@
 
 namespace b200fa {
 
-constexpr int kBlockM = 128;    // query rows per tile (per CTA)
+constexpr int kBlockM = 128;    // query rows per unit (per CTA)
 constexpr int kBlockN = 128;    // keys per KV block
 constexpr int kHeadDim = 128;   // head dimension (fixed)
 constexpr int kPairKeys = kBlockN / 2;    // K rows of a block held by each CTA
 constexpr int kPairDims = kHeadDim / 2;   // V head-dim columns held by each CTA
-constexpr int kItemUnits = 4;   // query units per work item (2 tiles x 2 CTAs)
-constexpr int kStages = 10;     // K/V ring depth (even: a slot only ever holds K or only V)
+constexpr int kItemUnits = 2;   // query units per work item (one per CTA)
+constexpr int kRing = 5;        // entries of the K ring and of the V ring (one stage each)
 constexpr int kQTileBytes = kBlockM * kHeadDim * 2;   // 32 KiB
 constexpr int kQHalfBytes = kQTileBytes / 2;          // TMA box: 64 cols x 128 rows
-constexpr int kKBoxRows = kPairKeys / 2;             // K rows of one S half held by each CTA
-constexpr int kKBoxBytes = kKBoxRows * 128;           // TMA box: 64 cols x 32 rows
-constexpr int kKPartBytes = 2 * kKBoxBytes;           // one S half's keys, all 128 columns
-constexpr int kStageBytes = 2 * kKPartBytes;          // 16 KiB
+constexpr int kKBoxRows = kPairKeys;                  // K rows of a block held by each CTA
+constexpr int kKBoxBytes = kKBoxRows * 128;           // TMA box: 64 cols x 64 rows
+constexpr int kStageBytes = 2 * kKBoxBytes;           // 16 KiB
 static_assert(kBlockN * kPairDims * 2 == kStageBytes, "K and V stages must have the same size");
-static_assert(kStages % 2 == 0, "ring slots must alternate K and V consistently");
-constexpr int kThreads = 384;    // 3 warpgroups
-constexpr int kMmaWarp = 8;      // tile t's issuer: warp kMmaWarp + 2t (rank 0)
+constexpr int kThreads = 384;      // 3 warpgroups
+constexpr int kSIssuerWarp = 8;    // rank 0: issues every S product
 constexpr int kLoadWarp = 9;
-constexpr int kForwardWarp = 11; // rank 1
+constexpr int kPVIssuerWarp = 10;  // rank 0: issues every PV product
+constexpr int kForwardWarp = 11;   // rank 1
 // Register split (setmaxnreg): launch 384 x 168 = 64512; softmax warpgroups
-// 256 x 208 + warpgroup 2 128 x 88 = 64512.
+// 256 x 192 + warpgroup 2 128 x 120 = 64512.  ptxas holds each region to its
+// share, so the control roles' 64-bit descriptors need the 120.
 constexpr uint32_t kLaunchRegs = 168;
-constexpr uint32_t kSoftmaxRegs = 208;
-constexpr uint32_t kControlRegs = 88;
+constexpr uint32_t kSoftmaxRegs = 192;
+constexpr uint32_t kControlRegs = 120;
 static_assert(256 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs, "register split exceeds the launch budget");
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (factor 256)
 
 // Tensor memory columns.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;       // + 128 t
-constexpr uint32_t kTmemO = 256;     // + 128 t
-constexpr uint32_t kTmemPLo = 96;    // column offset within S_t of P for keys 0-63
-constexpr uint32_t kTmemPHi = 64;    // column offset within S_t of P for keys 64-127
-static_assert(kTmemO + 256 <= kTmemCols, "TMEM budget");
+constexpr uint32_t kTmemO = 0;       // O, 128 columns
+constexpr uint32_t kTmemP = 128;     // + 64 b: P buffer b (FP16 pairs, 64 columns)
+constexpr uint32_t kTmemS = 256;     // + 128 b: S buffer b (FP32, 128 columns)
+static_assert(kTmemS + 2 * 128 <= kTmemCols, "TMEM budget");
 
 // Barrier slots.  "rank 0" barriers are only waited on in rank 0.
 constexpr int kBarQFull = 0;     // [2] Q tile landed (rank 0: own TMA + rank 1's forward; rank 1: own TMA)
-constexpr int kBarQEmpty = 2;    // [2] Q buffer free (epilogue store read it)                    local
-constexpr int kBarSLo = 4;       // [2] S_t keys 0-63 of a block computed   (pair commit to both CTAs)
-constexpr int kBarPHalf = 6;     // [2] rank 0: P_t keys 0-63 written by the 8 softmax warps of tile t
-constexpr int kBarPFull = 8;     // [2] rank 0: P_t keys 64-127 written (and O_t rescaled)
-constexpr int kBarOStaged = 10;  // [2] O tile staged in smem (128 threads)                       local
-constexpr int kBarDrain = 12;    // [2] rank 0: MMA drain of issuer t at exit
-constexpr int kBarOFinal = 14;   // [2] last PV_t of an item done   (pair commit to both CTAs)
-constexpr int kBarSHi = 16;      // [2] S_t keys 64-127 of a block computed (pair commit to both CTAs)
-constexpr int kBarKVFull = 18;   // [kStages] (rank 0: own TMA + rank 1's forward)
-constexpr int kBarKVEmpty = kBarKVFull + kStages;  // [kStages] released by both tiles' softmax   local
-constexpr int kNumBars = kBarKVEmpty + kStages;
-constexpr uint32_t kTileWarps = 8;  // softmax warps per tile in the pair (arrivals on P half / P full)
+constexpr int kBarQEmpty = 2;    // [2] Q tile free (the epilogue's store read it)                local
+constexpr int kBarSFull = 4;     // [2] S buffer b computed                    (S issuer commit to both CTAs)
+constexpr int kBarSFree = 6;     // [2] rank 0: S buffer b read by one group's 4 warps in each CTA
+constexpr int kBarPFull = 8;     // [2] rank 0: P buffer b written by one group's 4 warps in each CTA
+constexpr int kBarPVDone = 10;   // [2] PV of P buffer b done; O holds every block so far (PV issuer commit)
+constexpr int kBarRef = 12;      // [2] reference maximum of block g published (g % 2; 4 warps)  local
+constexpr int kBarXchg = 14;     // [1] epilogue row-sum exchange (8 warps)                        local
+constexpr int kBarOStaged = 15;  // [1] O tile staged in smem (8 warps)                            local
+constexpr int kBarDrain = 16;    // [2] rank 0: MMA drain of the S / PV issuer at exit
+constexpr int kBarKFull = 18;    // [kRing] K stage landed (rank 0: own TMA + rank 1's forward)
+constexpr int kBarKEmpty = kBarKFull + kRing;   // [kRing] S of its block done (S issuer commit to both CTAs)
+constexpr int kBarVFull = kBarKEmpty + kRing;   // [kRing] V stage landed (rank 0: own TMA + rank 1's forward)
+constexpr int kBarVEmpty = kBarVFull + kRing;   // [kRing] PV of its block done (PV issuer commit to both CTAs)
+constexpr int kNumBars = kBarVEmpty + kRing;
+constexpr uint32_t kGroupWarps = 8;  // one group's warps in the pair (arrivals on "S free" / "P full")
 
 constexpr int kSmemQ = 0;
-constexpr int kSmemKV = 2 * kQTileBytes;
-constexpr int kSmemBar = kSmemKV + kStages * kStageBytes;
-constexpr int kSmemMisc = kSmemBar + kNumBars * 8;  // TMEM base (4 B), abort flag (4 B)
-constexpr int kSmemUsed = kSmemMisc + 16;
+constexpr int kSmemK = 2 * kQTileBytes;
+constexpr int kSmemV = kSmemK + kRing * kStageBytes;
+constexpr int kSmemBar = kSmemV + kRing * kStageBytes;
+constexpr int kSmemXchg = kSmemBar + kNumBars * 8;        // float [2][128] reference / row-sum exchange
+constexpr int kSmemMisc = kSmemXchg + 2 * kBlockM * 4;    // TMEM base, abort flag, 6 block counters
+constexpr int kSmemUsed = kSmemMisc + 8 + 4 * 6;
 constexpr int kSmemBytes = kSmemUsed + 1024;  // + slack for 1024-B alignment
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 static_assert(kSmemBar % 8 == 0, "mbarrier alignment");
@@ -152,10 +149,11 @@ static_assert(kKBoxBytes % 1024 == 0 && kStageBytes % 1024 == 0, "128-byte swizz
 // tcgen05 instruction descriptors, kind::f16 (PTX ISA "Instruction
 // descriptor"): bits 4-5 D format (1 = F32), 7-9 A format (0 = F16),
 // 10-12 B format (0 = F16), 15 A major (0 = K), 16 B major (1 = MN),
-// 17-22 N>>3, 24-28 M>>4.  M = 256: the pair's rows.
-constexpr uint32_t kIdescQK = (1u << 4) | (uint32_t((kBlockN / 2) >> 3) << 17) | (uint32_t(256 >> 4) << 24);
+// 17-22 N>>3, 24-28 M>>4.  M = 256: the pair's rows; N = 128 for both
+// products (S: the block's keys, 64 per CTA; PV: the head dims, 64 per CTA).
+constexpr uint32_t kIdescQK = (1u << 4) | (uint32_t(kBlockN >> 3) << 17) | (uint32_t(256 >> 4) << 24);
 constexpr uint32_t kIdescPV = (1u << 4) | (1u << 16) | (uint32_t(kHeadDim >> 3) << 17) | (uint32_t(256 >> 4) << 24);
-static_assert((kBlockN / 2) % 16 == 0 && kBlockN <= 256, "M=256 needs N a multiple of 16");
+static_assert(kBlockN % 16 == 0 && kBlockN <= 256, "M=256 needs N a multiple of 16");
 
 // Shared-memory matrix descriptors (PTX ISA "Matrix Descriptor"), 128-byte
 // swizzle, sm_100 version bit.  Low word: start address >> 4 (bits 0-13),
@@ -164,9 +162,13 @@ static_assert((kBlockN / 2) % 16 == 0 && kBlockN <= 256, "M=256 needs N a multip
 // Rows of 128 B, 8-row groups 1024 B apart (SBO) for Q, K (K-major) and V
 // (MN-major: rows are keys, 64 head-dim columns per row).  The leading
 // offset is unused: swizzled K-major layouts ignore it and each CTA's V
-// half is a single 64-column block; it is set to 16 B.
+// half is a single 64-column block; it is set to 16 B.  Offsets added to a
+// descriptor's start address never carry out of bits 0-13: shared addresses
+// are below 256 KiB.
 constexpr uint32_t kDescHi = uint32_t(1024 >> 4) | (1u << 14) | (2u << 29);
-__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr) { return ((saddr & 0x3FFFFu) >> 4) | (1u << 16); }
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+  return (uint64_t(kDescHi) << 32) | uint64_t(((saddr & 0x3FFFFu) >> 4) | (1u << 16));
+}
 
 // exp2 on the FMA pipe for two lanes.  Cody-Waite split x = n + f with
 // n = round(x) taken from the low mantissa bits of x + 1.5*2^23 and
@@ -175,10 +177,23 @@ __device__ __forceinline__ uint32_t desc_lo(uint32_t saddr) { return ((saddr & 0
 // the exponent field as an integer.  x is clamped at -120 first so the
 // exponent cannot wrap; 2^-120 is 0 in FP16 and negligible in the FP32 row
 // sum, and masked keys (x = -inf) land there too.
-// Of every 8 key pairs, these go to the polynomial (measured per variant:
-// the FP32 variant's packed FP32 sums already load the FMA pipe).
+// Of every 8 key pairs, these go to the polynomial (a compile-time tuning
+// parameter per variant).
+#ifndef B200FA_POLY_PAIRS_FP16
+#define B200FA_POLY_PAIRS_FP16 2
+#endif
+#ifndef B200FA_POLY_PAIRS_FP32
+#define B200FA_POLY_PAIRS_FP32 1
+#endif
 template <int kVariant>
-constexpr int kPolyPairsOf = kVariant == 0 ? 2 : 1;
+constexpr int kPolyPairsOf = kVariant == 0 ? B200FA_POLY_PAIRS_FP16 : B200FA_POLY_PAIRS_FP32;
+// FP16 variant: MUFU exponentials of FP16 arguments in packed pairs (the
+// reference FP16 kernel's exp in FP16) instead of FP32 exponentials rounded
+// to FP16 (compile-time option).
+#ifndef B200FA_FP16_EXP_HALF2
+#define B200FA_FP16_EXP_HALF2 0
+#endif
+constexpr bool kExpHalf2 = B200FA_FP16_EXP_HALF2 != 0;
 constexpr float kExp2C0 = 0.9999280571937561f;
 constexpr float kExp2C1 = 0.6932609677314758f;
 constexpr float kExp2C2 = 0.2426111251115799f;
@@ -206,7 +221,7 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
 
 struct FwdParams {
   CUtensorMap tm_q;  // (128, Nq, B*Hq)  fp16, box (64, 128, 1), 128-B swizzle
-  CUtensorMap tm_k;  // (128, Nk, B*Hkv)       box (64, 32, 1)
+  CUtensorMap tm_k;  // (128, Nk, B*Hkv)       box (64, 64, 1)
   CUtensorMap tm_v;  // (128, Nk, B*Hkv)       box (64, 128, 1)
   CUtensorMap tm_o;  // (128, Nq, B*Hq)        box (64, 128, 1)
   int32_t Hq, Hkv, group;   // group = Hq / Hkv
@@ -228,29 +243,50 @@ constexpr uint32_t kFlagTrace = 1u;
 constexpr uint32_t kFlagTestWithholdP = 2u;
 constexpr uint32_t kFlagTimeline = 4u;
 constexpr uint32_t kFlagCapture = 8u;
+constexpr uint32_t kFlagTestBounds = 16u;  // checking build: one planted out-of-range coordinate
 
-// Debug timeline (kFlagTimeline): CTA 0 (rank 0 of the first pair) stamps
-// clock64() at fixed points of its first work item's first kTimelineBlocks
-// key blocks.  Layout: u64 [role][block][event] at byte kTimelineOffset of
-// the workspace; roles 0/1 = softmax tile 0/1 (warp 4t, lane 0), 2 = MMA
-// threads, 3 = TMA thread.  Softmax events: 0 S low ready, 1 keys 0-63
-// loaded, 2 row max / rescale decided, 3 P half handed over, 4 P full handed
-// over.  MMA events of tile t's issuer at 4t + {0 iteration start, 1 "P
-// half" seen, 2 "P full" seen, 3 second window issued}.  TMA events: 0/1 K
-// wait/issue, 2/3 V wait/issue.
+// Checking build (B200FA_DEBUG): coordinates, indices and layout are
+// verified before use and the roles' block counts at exit; a violation is
+// recorded as one of these status codes and takes the abort path.
+#ifdef B200FA_DEBUG
+constexpr bool kDebug = true;
+#else
+constexpr bool kDebug = false;
+#endif
+constexpr uint32_t kDevTimeout = 1u;
+constexpr uint32_t kDevBounds = 2u;
+constexpr uint32_t kDevPhase = 3u;
+constexpr uint32_t kCheckSite = 0x80u;  // low byte of a check's site: 0x80 + check number
+
+// Debug timeline (kFlagTimeline): both CTAs of the first pair stamp
+// clock64() at fixed points of their first work item's first kTimelineBlocks
+// key blocks.  Layout: u64 [rank][role][block][event] at byte
+// kTimelineOffset of the workspace; roles 0/1 = softmax group 0/1 (warp 4g;
+// each stamps its own blocks), 2 = rank 0's issuers / rank 1's forwarder,
+// 3 = TMA thread.  Softmax events: 0 scores ready seen, 1 scores loaded and
+// maximum reduced, 2 reference decided, 3 exponentials done, 4-7 P handed
+// over by the group's warps 0-3.  Issuer events: 0/1 PV started/issued, 2/3
+// S started/issued, 4 "S free" seen; forwarder events: 5/6 K/V forwarded.
+// TMA events: 0/1 K wait/issue, 2/3 V wait/issue.
 constexpr int kTimelineBlocks = 48;
 constexpr uint32_t kTimelineOffset = 256u + 32u * 1024u;
 
+// The recorder keeps one predicate; the address is recomputed from the
+// kernel parameters at each stamp, so a role's loop holds no pointer for it.
 struct Timeline {
-  uint64_t* base;  // nullptr when not recording
+  const FwdParams* p;
+  bool on;
   __device__ __forceinline__ void mark(int role, int j, int e) const {
-    if (base != nullptr && j < kTimelineBlocks) base[(role * kTimelineBlocks + j) * 8 + e] = clock64();
+    if (on && j < kTimelineBlocks) {
+      uint64_t* base = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p->ws) + kTimelineOffset) +
+                       cluster_rank() * (4u * kTimelineBlocks * 8u);
+      base[(role * kTimelineBlocks + j) * 8 + e] = clock64();
+    }
   }
 };
 
-__device__ __forceinline__ Timeline make_timeline(const FwdParams& p, int it) {
-  const bool on = (p.flags & kFlagTimeline) != 0 && blockIdx.x == 0 && it == 0;
-  return Timeline{on ? reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p.ws) + kTimelineOffset) : nullptr};
+__device__ __forceinline__ Timeline make_timeline(const FwdParams& p, int it, bool thread = true) {
+  return Timeline{&p, thread && (p.flags & kFlagTimeline) != 0 && cluster_id_x() == 0 && it == 0};
 }
 
 template <typename I>
@@ -304,17 +340,17 @@ __host__ __device__ inline void plan_decode(I nqb, I ub, I ue, I x, I& bh, I& qb
 }
 
 // Bounded mbarrier waits.  `site` identifies the wait in the status word:
-// (rank << 16) | (warp << 8) | barrier slot.
+// (rank << 16) | (warp << 8) | barrier slot (or kCheckSite + check number).
 struct Waiter {
   uint32_t abort_slot;       // shared u32, nonzero once any thread of the pair gave up
   uint32_t peer_abort_slot;  // the other CTA's abort flag (cluster address)
   uint64_t timeout_ns;
   uint32_t* ws;
 
-  __device__ __forceinline__ void fail(uint32_t site) const {
+  __device__ __forceinline__ void fail(uint32_t site, uint32_t code = kDevTimeout) const {
     st_volatile_shared(abort_slot, 1u);
     st_cluster_u32(peer_abort_slot, 1u);
-    if (atomicCAS(&ws[0], 0u, 1u /* B200FA_DEV_TIMEOUT */) == 0u) {
+    if (atomicCAS(&ws[0], 0u, code) == 0u) {
       ws[1] = site;
       ws[2] = blockIdx.x;
     }
@@ -343,6 +379,18 @@ struct Waiter {
     }
   }
 
+  // Checking build: false (after recording B200FA_DEV_BOUNDS with `site`
+  // and raising the abort flags) when `ok` is false; the product build
+  // compiles the check away.
+  __device__ __forceinline__ bool check(bool ok, uint32_t site) const {
+    if constexpr (kDebug) {
+      if (!ok) fail(site, kDevBounds);
+      return ok;
+    } else {
+      return true;
+    }
+  }
+
   // Exit-path wait for work this thread already issued (copies, MMAs); it
   // ignores the abort flag and gives up after `limit_ns`.
   __device__ __forceinline__ void drain(uint32_t bar, uint32_t parity, uint64_t limit_ns) const {
@@ -357,114 +405,162 @@ struct Smem {
   uint32_t base;  // shared-window address of the aligned base
   __device__ __forceinline__ uint32_t bar(int i) const { return base + kSmemBar + 8 * i; }
   __device__ __forceinline__ uint32_t q(int t) const { return base + kSmemQ + t * kQTileBytes; }
-  __device__ __forceinline__ uint32_t kv(uint32_t s) const { return base + kSmemKV + s * kStageBytes; }
+  __device__ __forceinline__ uint32_t k(uint32_t e) const { return base + kSmemK + e * kStageBytes; }
+  __device__ __forceinline__ uint32_t v(uint32_t e) const { return base + kSmemV + e * kStageBytes; }
+  __device__ __forceinline__ uint32_t xchg(uint32_t slot, int row) const {
+    return base + kSmemXchg + (slot * kBlockM + uint32_t(row)) * 4u;
+  }
   __device__ __forceinline__ uint32_t tmem_slot() const { return base + kSmemMisc; }
   __device__ __forceinline__ uint32_t abort_slot() const { return base + kSmemMisc + 4; }
+  // Checking build: key blocks counted by role r (0 S issuer, 1 PV issuer,
+  // 2 producer, 3 forwarder, 4/5 softmax group 0/1) at exit.
+  __device__ __forceinline__ uint32_t count_slot(int r) const { return base + kSmemMisc + 8 + 4 * r; }
 };
 
-// Positions in the K/V ring count the CTA's key blocks over all its items:
-// K of block g at 2g, V at 2g+1; slot = pos % kStages, use = pos / kStages.
-__device__ __forceinline__ uint32_t ring_slot(uint32_t pos) { return pos % kStages; }
-__device__ __forceinline__ uint32_t ring_parity(uint32_t pos) { return (pos / kStages) & 1u; }
+// The CTA counts its key blocks over all its items: block g has its K in K
+// ring entry g % kRing, its V in V ring entry g % kRing (the (g / kRing)-th
+// use of each), its scores in S buffer g % 2 and its P in P buffer g % 2.
+__device__ __forceinline__ uint32_t ring_entry(uint32_t g) { return g % kRing; }
+__device__ __forceinline__ uint32_t ring_parity(uint32_t g) { return (g / kRing) & 1u; }
+__device__ __forceinline__ uint32_t buf(uint32_t g) { return g & 1u; }
+__device__ __forceinline__ uint32_t buf_parity(uint32_t g) { return (g >> 1) & 1u; }
+
+// S = Q K^T over the 128 head dims (8 K=16 steps).  A = Q (two 64-column
+// halves kQHalfBytes apart), B = a K stage (two 64-column boxes kKBoxBytes
+// apart); step kk starts at half kk/4, 32 bytes per step within a half.
+__device__ __forceinline__ void issue_s(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint64_t a = q_desc + uint64_t((kk >> 2) * (kQHalfBytes >> 4) + (kk & 3) * 2);
+    const uint64_t b = k_desc + uint64_t((kk >> 2) * (kKBoxBytes >> 4) + (kk & 3) * 2);
+    mma_pair_ss(d_tmem, a, b, kIdescQK, kk > 0 ? 1u : 0u);
+  }
+}
+
+// O (+)= P V over the block's 128 keys (8 K=16 steps): A = P from TMEM (8
+// columns per step), B = a V stage (MN-major, 16 keys = 2 KiB per step).
+// acc = 0 overwrites O with the first step.
+__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint64_t v_desc, uint32_t acc) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    mma_pair_ts(o_tmem, p_tmem + 8u * uint32_t(kk), v_desc + uint64_t(kk * 128), kIdescPV, kk > 0 ? 1u : acc);
+}
 
 // ------------------------------------------------------------------ roles
-// Rank 0, one thread per tile: the pair's tensor-core work for tile t.
-// Timeline events (role 2): issuer t uses events 4t .. 4t+3.
-__device__ void mma_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base, const Waiter& w, int t) {
-  const uint32_t site = uint32_t(kMmaWarp + 2 * t) << 8;
+// Rank 0, one thread: every S = Q K^T product of the pair, block by block,
+// into S buffer g % 2 once the softmax has read block g - 2's scores from it.
+// After each product it commits "S full" on the buffer and the release of
+// the block's K stage, both multicast to the two CTAs.
+__device__ void s_issuer_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base, const Waiter& w) {
+  const uint32_t site = uint32_t(kSIssuerWarp) << 8;
   const int n = p.n_kv;
-  const uint32_t q_lo = desc_lo(sm.q(t));
-  const uint32_t ring_lo = desc_lo(sm.kv(0));   // + slot * (kStageBytes >> 4)
-  const uint32_t tS = tmem_base + kTmemS + 128u * t;
-  const uint32_t tO = tmem_base + kTmemO + 128u * t;
-  uint32_t kv_base = 0;   // ring position of the current item's K_0
-  uint32_t p_phase = 0;   // parity of "P half" / "P full" t
+  uint32_t g = 0;  // the CTA's key blocks so far
   bool ok = true;
-
-  auto kv_ready = [&](uint32_t pos) -> bool {
-    return w.wait(sm.bar(kBarKVFull + ring_slot(pos)), ring_parity(pos), site | kBarKVFull);
-  };
-  auto stage_lo = [&](uint32_t pos) -> uint32_t { return ring_lo + ring_slot(pos) * uint32_t(kStageBytes >> 4); };
-  // One half (keys 0-63: h = 0, keys 64-127: h = 1) of S_t = Q_t K^T for
-  // the block whose K sits at ring position `pos`, into S_t columns
-  // [64h, 64h+64); each CTA supplies 32 keys of the half.
-  auto issue_s_half = [&](uint32_t pos, int h) {
-    mma_pair_ss_k128<uint32_t(kQHalfBytes >> 4), uint32_t(kKBoxBytes >> 4)>(
-        tS + 64u * uint32_t(h), q_lo, stage_lo(pos) + uint32_t(h) * uint32_t(kKPartBytes >> 4), kDescHi, kIdescQK);
-    mma_commit_pair_both(sm.bar((h == 0 ? kBarSLo : kBarSHi) + t));
-  };
-
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
     const Timeline tl = make_timeline(p, it);
-    const uint32_t ip = uint32_t(it) & 1u;
-    if (!w.wait(sm.bar(kBarQFull + t), ip, site | (kBarQFull + t))) break;
-    if (!kv_ready(kv_base)) break;
-    tc_fence_after();
-    issue_s_half(kv_base, 0);  // S_t(0)
-    issue_s_half(kv_base, 1);
-    for (int j = 0; j < n; ++j) {
-      const uint32_t vpos = kv_base + 2u * uint32_t(j) + 1u;
-      const bool more = j + 1 < n;
-      tl.mark(2, j, 4 * t + 0);
-      // Both stages first: after each PV half this thread touches no shared
-      // memory before the S half that reuses its P columns.
-      if (!kv_ready(vpos) || (more && !kv_ready(vpos + 1u))) { ok = false; break; }
-      if (!w.wait(sm.bar(kBarPHalf + t), p_phase, site | (kBarPHalf + t))) { ok = false; break; }
-      tl.mark(2, j, 4 * t + 1);
+    const int qt = it & 1;
+    const uint64_t q_desc = smem_desc(sm.q(qt));
+    if (!w.wait(sm.bar(kBarQFull + qt), uint32_t(it >> 1) & 1u, site | uint32_t(kBarQFull + qt))) break;
+    for (int j = 0; j < n; ++j, ++g) {
+      const uint32_t b = buf(g), e = ring_entry(g);
+      if (g >= 2 && !w.wait(sm.bar(kBarSFree + int(b)), buf_parity(g - 2u), site | uint32_t(kBarSFree + int(b)))) {
+        ok = false;
+        break;
+      }
+      tl.mark(2, j, 4);
+      if (!w.wait(sm.bar(kBarKFull + int(e)), ring_parity(g), site | uint32_t(kBarKFull + int(e)))) {
+        ok = false;
+        break;
+      }
+      tl.mark(2, j, 2);
       tc_fence_after();
-      // "P half": S_t(j) keys 0-63 are read (P sits in the upper columns),
-      // so S_t(j+1) keys 0-63 go first and are ready early.
-      if (more) issue_s_half(vpos + 1u, 0);
-      mma_pair_ts_k64(tO, tS + kTmemPLo, stage_lo(vpos), kDescHi, kIdescPV, j == 0 ? 0u : 1u);
-      if (!w.wait(sm.bar(kBarPFull + t), p_phase, site | (kBarPFull + t))) { ok = false; break; }
-      p_phase ^= 1u;
-      tl.mark(2, j, 4 * t + 2);
-      tc_fence_after();
-      mma_pair_ts_k64(tO, tS + kTmemPHi, stage_lo(vpos) + 4u * 128u, kDescHi, kIdescPV, 1u);
-      if (more) issue_s_half(vpos + 1u, 1);  // keys 64-127, over both P halves: after both PV halves
-      else mma_commit_pair_both(sm.bar(kBarOFinal + t));
-      tl.mark(2, j, 4 * t + 3);
+      issue_s(tmem_base + kTmemS + 128u * b, q_desc, smem_desc(sm.k(e)));
+      mma_commit_pair_both(sm.bar(kBarSFull + int(b)));
+      mma_commit_pair_both(sm.bar(kBarKEmpty + int(e)));
+      tl.mark(2, j, 3);
     }
-    kv_base += 2u * uint32_t(n);
   }
+  if constexpr (kDebug) st_volatile_shared(sm.count_slot(0), g);
   // All MMAs this thread issued must be complete before TMEM is freed.
-  mma_commit_pair(sm.bar(kBarDrain + t));
-  w.drain(sm.bar(kBarDrain + t), 0u, 100000000ull);
+  mma_commit_pair(sm.bar(kBarDrain + 0));
+  w.drain(sm.bar(kBarDrain + 0), 0u, 100000000ull);
+}
+
+// Rank 0, one thread: every O += P V product of the pair, in block order
+// (so O accumulates in order and the item's first product, which overwrites
+// O, comes first).  After PV of block g it commits "PV done" on P buffer
+// g % 2 (the buffer may be rewritten, and O holds every block up to g) and
+// the release of the block's V stage.
+__device__ void pv_issuer_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base, const Waiter& w) {
+  const uint32_t site = uint32_t(kPVIssuerWarp) << 8;
+  const int n = p.n_kv;
+  uint32_t g = 0;
+  bool ok = true;
+  for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
+    const Timeline tl = make_timeline(p, it);
+    for (int j = 0; j < n; ++j, ++g) {
+      const uint32_t b = buf(g), e = ring_entry(g);
+      if (!w.wait(sm.bar(kBarVFull + int(e)), ring_parity(g), site | uint32_t(kBarVFull + int(e)))) {
+        ok = false;
+        break;
+      }
+      if (!w.wait(sm.bar(kBarPFull + int(b)), buf_parity(g), site | uint32_t(kBarPFull + int(b)))) {
+        ok = false;
+        break;
+      }
+      tl.mark(2, j, 0);
+      tc_fence_after();
+      issue_pv(tmem_base + kTmemO, tmem_base + kTmemP + 64u * b, smem_desc(sm.v(e)), j > 0 ? 1u : 0u);
+      mma_commit_pair_both(sm.bar(kBarPVDone + int(b)));
+      mma_commit_pair_both(sm.bar(kBarVEmpty + int(e)));
+      tl.mark(2, j, 1);
+    }
+  }
+  if constexpr (kDebug) st_volatile_shared(sm.count_slot(1), g);
+  mma_commit_pair(sm.bar(kBarDrain + 1));
+  w.drain(sm.bar(kBarDrain + 1), 0u, 100000000ull);
 }
 
 // Rank 1, one thread: replays the producer's sequence and, as each of this
 // CTA's stages lands, arrives on the same barrier of rank 0 (whose MMAs read
-// both CTAs' halves).
+// both CTAs' halves).  The arrival is relaxed: the stage's bytes are already
+// in this CTA's shared memory (this thread observed their completion on the
+// local barrier), and a cluster-scope release -- which orders this thread's
+// own earlier memory effects, of which there are none to order here -- took
+// about a thousand cycles per arrival under load, enough to pace the whole
+// pair at one block per two thousand cycles.
 __device__ void forward_role(const FwdParams& p, const Smem& sm, const Waiter& w) {
   const uint32_t site = (1u << 16) | (uint32_t(kForwardWarp) << 8);
   const int n = p.n_kv;
-  uint32_t pos = 0;
+  uint32_t g = 0;
   auto forward = [&](int bar, uint32_t parity) -> bool {
     if (!w.wait(sm.bar(bar), parity, site | uint32_t(bar))) return false;
-    mbar_arrive_cluster(map_shared(sm.bar(bar), 0));
+    mbar_arrive_cluster_relaxed(map_shared(sm.bar(bar), 0));
     return true;
   };
   bool ok = true;
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
-    const uint32_t ip = uint32_t(it) & 1u;
-    if (!forward(kBarQFull + 0, ip)) break;
-    for (int j = 0; j < n; ++j) {
-      if (!forward(kBarKVFull + int(ring_slot(pos)), ring_parity(pos))) { ok = false; break; }
-      ++pos;
-      if (j == 0 && !forward(kBarQFull + 1, ip)) { ok = false; break; }
-      if (!forward(kBarKVFull + int(ring_slot(pos)), ring_parity(pos))) { ok = false; break; }
-      ++pos;
+    const Timeline tl = make_timeline(p, it);
+    if (!forward(kBarQFull + (it & 1), uint32_t(it >> 1) & 1u)) break;
+    for (int j = 0; j < n; ++j, ++g) {
+      const int e = int(ring_entry(g));
+      if (!forward(kBarKFull + e, ring_parity(g))) { ok = false; break; }
+      tl.mark(2, j, 5);
+      if (!forward(kBarVFull + e, ring_parity(g))) { ok = false; break; }
+      tl.mark(2, j, 6);
     }
   }
+  if constexpr (kDebug) st_volatile_shared(sm.count_slot(3), g);
 }
 
-// Both ranks, one thread: this CTA's Q tiles and its halves of every K/V block.
+// Both ranks, one thread: this CTA's Q tiles and its halves of every K/V
+// block, K and V each into their own ring.
 __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, uint32_t rank) {
   const uint32_t site = (rank << 16) | (uint32_t(kLoadWarp) << 8);
   const int n = p.n_kv;
-  uint32_t kv_it = 0;
-  uint32_t issued = 0;       // bit s: stage s has ever been loaded
-  uint32_t last_par = 0;     // bit s: parity of stage s's last load
+  uint32_t g = 0;
+  uint32_t issued = 0;       // bit e / kRing + e: K / V entry e has ever been loaded
+  uint32_t last_par = 0;     // the same bits: parity of its last load
   uint32_t q_issued = 0, q_par = 0;
   bool ok = true;
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
@@ -472,60 +568,70 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, u
     plan_decode<int>(p.nqb, p.unit_begin, p.unit_end, item, bh, qb, cnt);
     const int b = bh / p.Hq;
     const int kvh = b * p.Hkv + (bh - b * p.Hq) / p.group;
-    // Tile t of rank r is unit 2t+r; missing units of a short item repeat
-    // the last one (computed, not stored).
-    const int u0 = int(rank) < cnt ? int(rank) : cnt - 1;
-    const int u1 = 2 + int(rank) < cnt ? 2 + int(rank) : cnt - 1;
-    const int row0 = (qb + u0) * kBlockM;
-    const int row1 = (qb + u1) * kBlockM;
-    const uint32_t ip = uint32_t(it) & 1u;
+    // Rank r holds unit r of the item; a one-unit item repeats it in rank 1
+    // (computed, not stored).
+    const int u = int(rank) < cnt ? int(rank) : cnt - 1;
+    const int row0 = (qb + u) * kBlockM;
+    const int qt = it & 1;
+    const uint32_t qp = uint32_t(it >> 1) & 1u;
     const Timeline tl = make_timeline(p, it);
-    if (!w.wait(sm.bar(kBarQEmpty + 0), ip ^ 1u, site | (kBarQEmpty + 0))) break;
-    mbar_arrive_expect_tx(sm.bar(kBarQFull + 0), kQTileBytes);
-    tma_load_3d(sm.q(0), &p.tm_q, sm.bar(kBarQFull + 0), 0, row0, bh);
-    tma_load_3d(sm.q(0) + kQHalfBytes, &p.tm_q, sm.bar(kBarQFull + 0), 64, row0, bh);
-    q_issued |= 1u;
-    q_par = (q_par & ~1u) | ip;
-    for (int j = 0; j < n; ++j) {
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {  // 0: K_j half, 1: V_j half
-        const uint32_t s = ring_slot(kv_it);
-        const uint32_t ph = ring_parity(kv_it);
-        ++kv_it;
-        tl.mark(3, j, 2 * which);
-        if (!w.wait(sm.bar(kBarKVEmpty + s), ph ^ 1u, site | (kBarKVEmpty + s))) { ok = false; break; }
-        tl.mark(3, j, 2 * which + 1);
-        mbar_arrive_expect_tx(sm.bar(kBarKVFull + s), kStageBytes);
-        if (which == 0) {  // keys [j*128 + 64h + 32r, +32) of each half h, all 128 head-dim columns
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int krow = j * kBlockN + h * (kBlockN / 2) + int(rank) * kKBoxRows;
-            const uint32_t dst = sm.kv(s) + uint32_t(h * kKPartBytes);
-            tma_load_3d(dst, &p.tm_k, sm.bar(kBarKVFull + s), 0, krow, kvh);
-            tma_load_3d(dst + kKBoxBytes, &p.tm_k, sm.bar(kBarKVFull + s), 64, krow, kvh);
-          }
-        } else {           // keys [j*128, +128), head-dim columns [64r, +64)
-          tma_load_3d(sm.kv(s), &p.tm_v, sm.bar(kBarKVFull + s), int(rank) * kPairDims, j * kBlockN, kvh);
-        }
-        issued |= 1u << s;
-        last_par = (last_par & ~(1u << s)) | (ph << s);
-        if (which == 0 && j == 0) {
-          if (!w.wait(sm.bar(kBarQEmpty + 1), ip ^ 1u, site | (kBarQEmpty + 1))) { ok = false; break; }
-          mbar_arrive_expect_tx(sm.bar(kBarQFull + 1), kQTileBytes);
-          tma_load_3d(sm.q(1), &p.tm_q, sm.bar(kBarQFull + 1), 0, row1, bh);
-          tma_load_3d(sm.q(1) + kQHalfBytes, &p.tm_q, sm.bar(kBarQFull + 1), 64, row1, bh);
-          q_issued |= 2u;
-          q_par = (q_par & ~2u) | (ip << 1);
-        }
+    const int kv_planes = p.heads / p.group;
+    const int row_end = p.nqb * kBlockM, key_end = p.n_kv * kBlockN;
+    // The item's plan: a head of the problem, one or two query blocks inside
+    // it and inside the unit range, a KV head of the problem.
+    if (!w.check(bh >= 0 && bh < p.heads && qb >= 0 && cnt >= 1 && cnt <= kItemUnits && qb + cnt <= p.nqb &&
+                     bh * p.nqb + qb >= p.unit_begin && bh * p.nqb + qb + cnt <= p.unit_end && kvh >= 0 &&
+                     kvh < kv_planes,
+                 site | (kCheckSite + 0u)))
+      break;
+    if (!w.wait(sm.bar(kBarQEmpty + qt), qp ^ 1u, site | uint32_t(kBarQEmpty + qt))) break;
+    // Q rows of the unit (x = 0 / 64: 16-byte aligned columns).
+    const int q_row = row0 + ((p.flags & kFlagTestBounds) ? row_end : 0);
+    if (!w.check(q_row >= 0 && q_row < row_end && row0 % kBlockM == 0, site | (kCheckSite + 1u))) break;
+    mbar_arrive_expect_tx(sm.bar(kBarQFull + qt), kQTileBytes);
+    tma_load_3d(sm.q(qt), &p.tm_q, sm.bar(kBarQFull + qt), 0, row0, bh);
+    tma_load_3d(sm.q(qt) + kQHalfBytes, &p.tm_q, sm.bar(kBarQFull + qt), 64, row0, bh);
+    q_issued |= 1u << qt;
+    q_par = (q_par & ~(1u << qt)) | (qp << qt);
+    for (int j = 0; j < n; ++j, ++g) {
+      const uint32_t e = ring_entry(g);
+      const uint32_t ph = ring_parity(g);
+      // K: keys [j*128 + 64r, +64), all 128 head-dim columns, as two 64-column
+      // boxes, once S of block g - kRing completed.
+      tl.mark(3, j, 0);
+      if (!w.wait(sm.bar(kBarKEmpty + int(e)), ph ^ 1u, site | (kBarKEmpty + e))) { ok = false; break; }
+      tl.mark(3, j, 1);
+      const int krow = j * kBlockN + int(rank) * kKBoxRows;
+      if (!w.check(krow >= 0 && krow + kKBoxRows <= key_end, site | (kCheckSite + 2u))) { ok = false; break; }
+      mbar_arrive_expect_tx(sm.bar(kBarKFull + int(e)), kStageBytes);
+      tma_load_3d(sm.k(e), &p.tm_k, sm.bar(kBarKFull + int(e)), 0, krow, kvh);
+      tma_load_3d(sm.k(e) + kKBoxBytes, &p.tm_k, sm.bar(kBarKFull + int(e)), 64, krow, kvh);
+      issued |= 1u << e;
+      last_par = (last_par & ~(1u << e)) | (ph << e);
+      // V: keys [j*128, +128), head-dim columns [64r, +64), once PV of block
+      // g - kRing completed.
+      tl.mark(3, j, 2);
+      if (!w.wait(sm.bar(kBarVEmpty + int(e)), ph ^ 1u, site | (kBarVEmpty + e))) { ok = false; break; }
+      tl.mark(3, j, 3);
+      if (!w.check(j * kBlockN + kBlockN <= key_end && int(rank) * kPairDims + kPairDims <= kHeadDim,
+                   site | (kCheckSite + 3u))) {
+        ok = false;
+        break;
       }
-      if (!ok) break;
+      mbar_arrive_expect_tx(sm.bar(kBarVFull + int(e)), kStageBytes);
+      tma_load_3d(sm.v(e), &p.tm_v, sm.bar(kBarVFull + int(e)), int(rank) * kPairDims, j * kBlockN, kvh);
+      issued |= 1u << (kRing + e);
+      last_par = (last_par & ~(1u << (kRing + e))) | (ph << (kRing + e));
     }
   }
+  if constexpr (kDebug) st_volatile_shared(sm.count_slot(2), g);
   // Copies still in flight must land before the CTA exits (only possible on
   // the abort path; on the normal path rank 0's MMAs consumed every stage).
   if (!ok || ld_volatile_shared(sm.abort_slot()) != 0u) {
-    for (int s = 0; s < kStages; ++s)
-      if (issued & (1u << s)) w.drain(sm.bar(kBarKVFull + s), (last_par >> s) & 1u, 50000000ull);
+    for (int e = 0; e < kRing; ++e) {
+      if (issued & (1u << e)) w.drain(sm.bar(kBarKFull + e), (last_par >> e) & 1u, 50000000ull);
+      if (issued & (1u << (kRing + e))) w.drain(sm.bar(kBarVFull + e), (last_par >> (kRing + e)) & 1u, 50000000ull);
+    }
     for (int t = 0; t < 2; ++t)
       if (q_issued & (1u << t)) w.drain(sm.bar(kBarQFull + t), (q_par >> t) & 1u, 50000000ull);
   }
@@ -534,14 +640,16 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, u
 // Exponentials of 16*kGroups keys (8 pairs per group) of one row:
 // x = s * scale*log2(e) - m with packed FP32 FMAs; of every 8 pairs the last
 // kPoly go through the FMA-pipe polynomial (exp2_poly2) and the rest through
-// MUFU (FP32 ex2).  Writes 8*kGroups packed FP16 pairs of P and adds the
-// row sum: FP32 variant, the FP32 exponentials into packed FP32 sums (four
+// MUFU (FP32 ex2, or for the FP16 variant with kExpHalf2 FP16 ex2 of the
+// packed pair).  Writes 8*kGroups packed FP16 pairs of P and adds the row
+// sum: FP32 variant, the FP32 exponentials into packed FP32 sums (four
 // chains, folded into acc0/acc1); FP16 variant, the FP16 P itself into
 // packed FP16 sums (four chains; at most 16*kGroups <= 64 terms of <= 2^8,
 // far inside FP16 range), carried over to FP32 once per call (hsum).
 template <int kVariant, int kPoly, int kGroups>
 __device__ __forceinline__ void exp_keys(const uint32_t* r, uint64_t sl2x2, uint64_t nmx2, uint32_t* pk,
                                          uint64_t& acc0, uint64_t& acc1, float& hsum) {
+  static_assert(kGroups <= 4, "FP16 partial sums cover at most 64 keys");
   uint64_t cacc[4] = {0ull, 0ull, 0ull, 0ull};
   uint32_t hc[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
@@ -550,19 +658,25 @@ __device__ __forceinline__ void exp_keys(const uint32_t* r, uint64_t sl2x2, uint
     for (int pp = 0; pp < 8; ++pp) {
       const int i = g * 8 + pp;  // key pair index
       const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sl2x2, nmx2);
-      uint64_t p2;
-      if (pp >= 8 - kPoly) {
-        p2 = exp2_poly2(x2);
-      } else {
+      if (kVariant == 0 && kExpHalf2 && pp < 8 - kPoly) {
         float a, b;
         f2_unpack(x2, a, b);
-        p2 = f2_pack(ex2_approx(a), ex2_approx(b));
+        pk[i] = ex2_approx_h2(pack_h2(a, b));
+      } else {
+        uint64_t p2;
+        if (pp >= 8 - kPoly) {
+          p2 = exp2_poly2(x2);
+        } else {
+          float a, b;
+          f2_unpack(x2, a, b);
+          p2 = f2_pack(ex2_approx(a), ex2_approx(b));
+        }
+        float ea, eb;
+        f2_unpack(p2, ea, eb);
+        pk[i] = pack_h2(ea, eb);
+        if constexpr (kVariant == 1) cacc[pp & 3] = f2_add(cacc[pp & 3], p2);
       }
-      float ea, eb;
-      f2_unpack(p2, ea, eb);
-      pk[i] = pack_h2(ea, eb);
-      if constexpr (kVariant == 1) cacc[pp & 3] = f2_add(cacc[pp & 3], p2);
-      else hc[pp & 3] = (g == 0 && pp < 4) ? pk[i] : hadd2(hc[pp & 3], pk[i]);
+      if constexpr (kVariant == 0) hc[pp & 3] = (g == 0 && pp < 4) ? pk[i] : hadd2(hc[pp & 3], pk[i]);
     }
   }
   if constexpr (kVariant == 0) hsum += h2_sum_f32(hadd2(hadd2(hc[0], hc[1]), hadd2(hc[2], hc[3])));
@@ -585,82 +699,106 @@ __device__ __forceinline__ float row_max64(const uint32_t* r) {
   return fmaxf(fmaxf(mc0, mc1), fmaxf(mc2, mc3));
 }
 
-// Keys at or beyond `valid` (the last block's key count) get score -inf.
-__device__ __forceinline__ void mask_keys64(uint32_t* r, int first_key, int valid) {
+// Keys at or beyond `valid` (the last block's key count) of 64 scores that
+// start at key `first` get score -inf.
+__device__ __forceinline__ void mask_keys64(uint32_t* r, int first, int valid) {
 #pragma unroll
   for (int i = 0; i < 64; ++i)
-    if (first_key + i >= valid) r[i] = __float_as_uint(-INFINITY);
+    if (first + i >= valid) r[i] = __float_as_uint(-INFINITY);
 }
 
-// Scores of keys [first, first+64) of this thread's row from TMEM.
-__device__ __forceinline__ void load_keys64(uint32_t tS, int first, uint32_t* r, bool tail, int valid) {
-  tmem_ld32(tS + uint32_t(first), r);
-  tmem_ld32(tS + uint32_t(first) + 32u, r + 32);
+// Scores of a block's 128 keys of this thread's row from TMEM; keys at or
+// beyond `valid` (the last block's key count) get score -inf.
+__device__ __forceinline__ void load_scores(uint32_t tS, uint32_t* r, bool tail, int valid) {
+  tmem_ld32(tS, r);
+  tmem_ld32(tS + 32u, r + 32);
+  tmem_ld32(tS + 64u, r + 64);
+  tmem_ld32(tS + 96u, r + 96);
   tmem_wait_ld();
-  if (tail) mask_keys64(r, first, valid);
+  if (tail) {
+    mask_keys64(r, 0, valid);
+    mask_keys64(r + 64, 64, valid);
+  }
 }
 
-// Softmax of one query tile per warpgroup (warps 0-3: tile 0, 4-7: tile 1),
-// one thread per query row (its TMEM lane), in both CTAs.
-// kCapture: the debug-capture instantiation (separate kernels, so the
-// production ones carry no capture code).
+// O row of this thread (128 FP32 columns in TMEM) times `f`, in place.
+__device__ __forceinline__ void scale_o_row(uint32_t tO, float f) {
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t o[32];
+    tmem_ld32(tO + 32u * uint32_t(c), o);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+    tmem_st32(tO + 32u * uint32_t(c), o);
+  }
+  tmem_wait_st();
+}
+
+// Softmax of the CTA's query unit: group grp (warps 4*grp .. 4*grp+3) takes
+// the item's key blocks j with j % 2 == grp, one thread per query row (its
+// TMEM lane), in both CTAs.  kCapture: the debug-capture instantiation
+// (separate kernels, so the production ones carry no capture code).
 template <int kVariant, bool kCapture>  // kVariant 0 = FP16 softmax, 1 = FP32 softmax
 __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_base, const Waiter& w,
                              uint32_t warp, uint32_t lane, uint32_t rank) {
-  const int t = int(warp >> 2);   // tile = warpgroup
-  const int wq = int(warp & 3);   // TMEM lane quarter of this warp
+  const int grp = int(warp >> 2);  // block parity this group takes
+  const int wq = int(warp & 3);    // TMEM lane quarter of this warp
   const int row = wq * 32 + int(lane);
   const uint32_t lane_off = uint32_t(wq * 32) << 16;
-  const uint32_t tS = tmem_base + lane_off + kTmemS + uint32_t(t) * 128;
-  const uint32_t tO = tmem_base + lane_off + kTmemO + uint32_t(t) * 128;
-  const uint32_t sQ = sm.q(t);
+  const uint32_t tO = tmem_base + lane_off + kTmemO;
   const uint32_t site = (rank << 16) | (warp << 8);
   const float sl2 = p.scale_log2;
   const uint64_t sl2x2 = f2_pack(sl2, sl2);
   const int n = p.n_kv;
-  const bool withhold = (p.flags & kFlagTestWithholdP) != 0 && t == 1;
-  // P half / P full live in rank 0; each warp arrives once (lane 0), after
-  // its TMEM writes completed (tcgen05.wait::st), so rank 1's remote
-  // arrival can be relaxed.
-  const uint32_t p_half = rank == 0 ? sm.bar(kBarPHalf + t) : map_shared(sm.bar(kBarPHalf + t), 0);
-  const uint32_t p_full = rank == 0 ? sm.bar(kBarPFull + t) : map_shared(sm.bar(kBarPFull + t), 0);
-  auto arrive_rank0 = [&](uint32_t bar) {
+  const bool withhold = (p.flags & kFlagTestWithholdP) != 0 && grp == 1;
+  constexpr int kPoly = kPolyPairsOf<kVariant>;
+  // "S free" and "P full" live in rank 0; each warp arrives once (lane 0),
+  // after its TMEM reads / writes completed (tcgen05.wait::ld / ::st), so
+  // rank 1's remote arrival can be relaxed.
+  auto arrive_rank0 = [&](int bar) {
     __syncwarp();
     if (lane == 0) {
-      if (rank == 0) mbar_arrive(bar);
-      else mbar_arrive_cluster_relaxed(bar);
+      if (rank == 0) mbar_arrive(sm.bar(bar));
+      else mbar_arrive_cluster_relaxed(map_shared(sm.bar(bar), 0));
     }
   };
-  // One thread per tile returns this tile's use of the K/V ring slots to
-  // the CTA's producer (a slot takes one arrival per tile): K of block g
-  // once "S high t" g completed, V of block g once "S high t" g+1 (or "O
-  // final t") completed.
-  const bool releaser = wq == 0 && lane == 0;
-  uint32_t g = 0;        // key blocks of this CTA so far (ring positions 2g, 2g+1)
-  uint32_t s_phase = 0;  // parity of "S low t" / "S high t"
+  auto arrive_local = [&](int bar) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(sm.bar(bar));
+  };
+  // Bounded wait with a warp-uniform outcome: the warp leaves together, so no
+  // warp-collective instruction (tcgen05.ld/st, __syncwarp) ever runs with
+  // part of the warp gone.
+  auto wait_warp = [&](int bar, uint32_t parity) -> bool {
+    return __all_sync(0xffffffffu, w.wait(sm.bar(bar), parity, site | uint32_t(bar)));
+  };
   bool ok = true;
+  uint32_t blocks_done = 0;  // checking build: this group's key blocks
 
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
-    float m_ref = -INFINITY;  // reference maximum, log2 domain
-    float l = 0.f;
-    const Timeline tl = (wq == 0 && lane == 0) ? make_timeline(p, it) : Timeline{nullptr};
-    // Debug capture: cap_on is warp-uniform (this tile holds a unit of the
-    // item), cap_row per thread (its query row exists).  Record (b*Hq+hq,
-    // block j, row) sits at index (bh*n + j)*nq + row of each scalar plane
-    // (stride heads*n*nq) and, times 128, in the O plane after them.
+    const uint32_t g0 = uint32_t(it) * uint32_t(n);  // the CTA's block count before this item
+    float m_cur = -INFINITY;  // reference of this group's last block (log2 domain)
+    float l_g = 0.f;          // this group's row sum over its blocks, relative to m_cur
+    const Timeline tl = make_timeline(p, it, wq == 0 && lane == 0);
+    const Timeline tl_warp = make_timeline(p, it, lane == 0);  // per-warp hand-off stamps
+    // Debug capture: cap_on (this CTA's unit exists in the item) is
+    // warp-uniform, cap_row per thread (its query row exists).  Record
+    // (b*Hq+hq, block j, row) sits at index (bh*n + j)*nq + row of each
+    // scalar plane (stride heads*n*nq) and, times 128, in the O plane after
+    // them.
     bool cap_on = false, cap_row = false;
     size_t cap_idx = 0;
     if constexpr (kCapture) {
       int bh, qb, cnt;
       plan_decode<int>(p.nqb, p.unit_begin, p.unit_end, item, bh, qb, cnt);
-      const int u = 2 * t + int(rank);
-      const int qrow = (qb + u) * kBlockM + row;
-      cap_on = u < cnt;
+      const int qrow = (qb + int(rank)) * kBlockM + row;
+      cap_on = int(rank) < cnt;
       cap_row = cap_on && qrow < p.nq;
       cap_idx = (size_t(bh) * size_t(n)) * size_t(p.nq) + size_t(qrow);
     }
     const size_t cap_plane = size_t(p.heads) * size_t(n) * size_t(p.nq);
-    // O after PV_t(jb) (unnormalised FP32, relative to that block's m):
+    // O after PV(jb) (unnormalised FP32, relative to that block's m):
     // read the row from TMEM (whole warp), store it.
     auto capture_o = [&](int jb) {
       float4* orec = reinterpret_cast<float4*>(p.capture + 4 * cap_plane +
@@ -678,115 +816,143 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
         }
       }
     };
+    // PV of block gp done (and, one issuer in order, every PV before it).
+    // The barrier's next phase is PV of block gp + 2, which cannot complete
+    // before this group's next "P full": no phase is missed.
+    auto wait_pv = [&](uint32_t gp) -> bool { return wait_warp(kBarPVDone + int(buf(gp)), buf_parity(gp)); };
 
-    for (int j = 0; j < n; ++j, ++g) {
-      // Keys 0-63 ("S low" j; it also means PV_t(j-1) keys 0-63 are done):
-      // load, exponentiate speculatively against the current reference
-      // (after the first block), and reduce their maximum.
-      if (!w.wait(sm.bar(kBarSLo + t), s_phase, site | (kBarSLo + t))) { ok = false; break; }
-      tl.mark(t, j, 0);
+    for (int j = grp; j < n; j += 2) {
+      const uint32_t gb = g0 + uint32_t(j);
+      const uint32_t b = buf(gb);
+      const uint32_t tS = tmem_base + lane_off + kTmemS + 128u * b;
+      const uint32_t tP = tmem_base + lane_off + kTmemP + 64u * b;
+      // Reference after block j-1 ("ref" gb-1, published by the other group
+      // about one block period earlier).  Waited for also at an item's
+      // first block (value unused): the wait orders this group's write of
+      // slot gb % 2 after the other group's read of it.
+      float m_prev = -INFINITY;
+      if (gb > 0) {
+        if (!wait_warp(kBarRef + int((gb - 1u) & 1u), ((gb - 1u) >> 1) & 1u)) {
+          ok = false;
+          break;
+        }
+        if (j > 0) m_prev = ld_shared_f32(sm.xchg((gb - 1u) & 1u, row));
+      }
+      if (!wait_warp(kBarSFull + int(b), buf_parity(gb))) {
+        ok = false;
+        break;
+      }
+      tl.mark(grp, j, 0);
       tc_fence_after();
       const bool tail = (j == n - 1 && p.nk_tail < kBlockN);
+      uint32_t r[kBlockN];
+      load_scores(tS, r, tail, p.nk_tail);
+      arrive_rank0(kBarSFree + int(b));  // the S issuer may refill the buffer
+      const float mx = fmaxf(row_max64(r), row_max64(r + 64)) * sl2;
+      tl.mark(grp, j, 1);
+      // This group's partial sum follows the reference the other group left.
+      if (j >= 2 && m_prev != m_cur) l_g *= ex2_approx(m_cur - m_prev);
+      float m_new = m_prev, alpha = 1.f;
+      bool moved = false;
+      if (mx > m_prev + kRescaleLog2) {
+        m_new = mx;
+        moved = j > 0;
+        alpha = ex2_approx(m_prev - mx);  // 0 at the item's first block
+      }
+      st_shared_f32(sm.xchg(gb & 1u, row), m_new);
+      arrive_local(kBarRef + int(gb & 1u));
+      tl.mark(grp, j, 2);
+      if constexpr (kCapture) {
+        if (cap_on && j > 0) {
+          if (!wait_pv(gb - 1u)) { ok = false; break; }
+          tc_fence_after();
+          capture_o(j - 1);
+        }
+      }
+      if (moved) l_g *= alpha;
+      m_cur = m_new;
       uint32_t pk[kBlockN / 2];
       uint64_t acc0 = 0ull, acc1 = 0ull;  // packed FP32 partial row sums
       float hsum = 0.f;                   // FP16 variant: sums of FP16 group sums
-      float mx;
-      {
-        uint32_t r[64];
-        load_keys64(tS, 0, r, tail, p.nk_tail);
-        tl.mark(t, j, 1);
-        if (j > 0) exp_keys<kVariant, kPolyPairsOf<kVariant>, 4>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
-        mx = row_max64(r);
-      }
-      // Keys 64-127 ("S high" j: S_t(j) and PV_t(j-1) complete): load and
-      // reduce (their exponentials follow the check).
-      if (!w.wait(sm.bar(kBarSHi + t), s_phase, site | (kBarSHi + t))) { ok = false; break; }
-      s_phase ^= 1u;
-      if (releaser) {
-        mbar_arrive(sm.bar(kBarKVEmpty + ring_slot(2u * g)));                  // S_t(j) read K_j
-        if (j > 0) mbar_arrive(sm.bar(kBarKVEmpty + ring_slot(2u * g - 1u)));  // PV_t(j-1) read V_(j-1)
-      }
-      tc_fence_after();
-      if constexpr (kCapture) {
-        if (cap_on && j > 0) capture_o(j - 1);
-      }
-      uint32_t r1[64];
-      load_keys64(tS, 64, r1, tail, p.nk_tail);
-      const float m_blk = fmaxf(mx, row_max64(r1)) * sl2;
-      float alpha = 1.f;
-      bool moved = false;
-      if (m_blk > m_ref + kRescaleLog2) {
-        alpha = ex2_approx(m_ref - m_blk);  // 0 on the first block
-        m_ref = m_blk;
-        moved = true;
-      }
-      l *= alpha;
-      tl.mark(t, j, 2);
+      const uint64_t nm = f2_pack(-m_new, -m_new);
+      exp_keys<kVariant, kPoly, 4>(r, sl2x2, nm, pk, acc0, acc1, hsum);
+      exp_keys<kVariant, kPoly, 4>(r + 64, sl2x2, nm, pk + 32, acc0, acc1, hsum);
+      tl.mark(grp, j, 3);
       if (__any_sync(0xffffffffu, moved)) {
-        // Lazy correction of the running output before any of this block's
-        // P is handed over (PV_t(j-1) is complete: "S high" j covers it;
-        // the P stores' wait below also covers these stores).  Then keys
-        // 0-63 again from S, which is intact until P is written.
-        if (j > 0) {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + 32 * c, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tO + 32 * c, o);
-          }
-        }
-        uint32_t r[64];
-        load_keys64(tS, 0, r, tail, p.nk_tail);
-        if (moved) {
-          acc0 = 0ull;
-          acc1 = 0ull;
-          hsum = 0.f;
-          exp_keys<kVariant, kPolyPairsOf<kVariant>, 4>(r, sl2x2, f2_pack(-m_ref, -m_ref), pk, acc0, acc1, hsum);
-        }
+        // Lazy correction of the running output before this block's P is
+        // handed over: PV(gb-1) must be complete (PV(gb) waits for "P full").
+        if (!wait_pv(gb - 1u)) { ok = false; break; }
+        tc_fence_after();
+        scale_o_row(tO, moved ? alpha : 1.f);
       }
-      tmem_st32(tS + kTmemPLo, pk);
-      tmem_wait_st();
-      tc_fence_before();
-      arrive_rank0(p_half);
-      tl.mark(t, j, 3);
-      exp_keys<kVariant, kPolyPairsOf<kVariant>, 4>(r1, sl2x2, f2_pack(-m_ref, -m_ref), pk + 32, acc0, acc1, hsum);
-      tmem_st32(tS + kTmemPHi, pk + 32);
-      tmem_wait_st();
-      tc_fence_before();
-      if (!(withhold && it == 0 && j == 0)) arrive_rank0(p_full);
-      tl.mark(t, j, 4);
       float a0, b0, a1, b1;
       f2_unpack(acc0, a0, b0);
       f2_unpack(acc1, a1, b1);
       const float z = ((a0 + b0) + (a1 + b1)) + hsum;
-      l += z;
+      l_g += z;
       if constexpr (kCapture) {
+        // Running row sum over both groups: the other group's record of
+        // block j-1 holds the total after it; it was written and fenced
+        // before that group's "P full", which PV(j-1) -- waited for above --
+        // follows.
         if (cap_row) {
           float* rec = p.capture + cap_idx + size_t(j) * size_t(p.nq);
-          rec[0] = m_ref;
-          rec[cap_plane] = l;
+          const float l_prev = j == 0 ? 0.f : ld_volatile_global_f32(rec + cap_plane - p.nq);
+          rec[0] = m_new;
+          rec[cap_plane] = (j == 0 ? 0.f : alpha * l_prev) + z;
           rec[2 * cap_plane] = j == 0 ? 0.f : alpha;
           rec[3 * cap_plane] = z;
         }
+        __threadfence();
       }
+      // P buffer b is free once PV of block gb - 2 completed.
+      if (gb >= 2 && !wait_pv(gb - 2u)) { ok = false; break; }
+      tc_fence_after();
+      tmem_st32(tP, pk);
+      tmem_st32(tP + 32u, pk + 32);
+      tmem_wait_st();
+      tc_fence_before();
+      if (!(withhold && it == 0 && j == 1)) arrive_rank0(kBarPFull + int(b));
+      ++blocks_done;
+      tl_warp.mark(grp, j, 4 + wq);
     }
     if (!ok) break;
 
-    // ---- epilogue: O / l -> FP16 -> swizzled smem (this tile's Q buffer) -> TMA store
-    if (!w.wait(sm.bar(kBarOFinal + t), uint32_t(it) & 1u, site | (kBarOFinal + t))) { ok = false; break; }
-    if (releaser) mbar_arrive(sm.bar(kBarKVEmpty + ring_slot(2u * g - 1u)));  // V of the item's last block
+    // ---- epilogue: O / l -> FP16 -> swizzled smem (this item's Q tile) -> TMA store.
+    // Group grp converts head-dim columns [64 grp, +64) of its rows.
+    const int qt = it & 1;
+    const uint32_t sQ = sm.q(qt);
+    const uint32_t g_last = g0 + uint32_t(n) - 1u;
+    if (!wait_pv(g_last)) { ok = false; break; }  // every PV of the item complete
     tc_fence_after();
-    if constexpr (kCapture) {
-      if (cap_on) capture_o(n - 1);
+    // Both partial sums to the final reference, then added.
+    float m_final = m_cur;
+    if ((n - 1) % 2 != grp) {
+      if (!wait_warp(kBarRef + int(g_last & 1u), (g_last >> 1) & 1u)) {
+        ok = false;
+        break;
+      }
+      m_final = ld_shared_f32(sm.xchg(g_last & 1u, row));
     }
+    if (l_g != 0.f && m_final != m_cur) l_g *= ex2_approx(m_cur - m_final);
+    if constexpr (kCapture) {
+      if (cap_on && grp == 0) capture_o(n - 1);
+    }
+    // Exchange through the two reference slots: phase 0 -- every reference
+    // read; group 0 writes slot g_last % 2 (which the other group's next
+    // write follows its own read of), group 1 the other; phase 1 -- read.
+    arrive_local(kBarXchg);
+    if (!wait_warp(kBarXchg, 0u)) { ok = false; break; }
+    const uint32_t mine = grp == 0 ? (g_last & 1u) : ((g_last + 1u) & 1u);
+    st_shared_f32(sm.xchg(mine, row), l_g);
+    arrive_local(kBarXchg);
+    if (!wait_warp(kBarXchg, 1u)) { ok = false; break; }
+    const float l = l_g + ld_shared_f32(sm.xchg(mine ^ 1u, row));
     const float inv_l = 1.f / l;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       uint32_t o[32];
-      tmem_ld32(tO + 32 * c, o);
+      tmem_ld32(tO + 64u * uint32_t(grp) + 32u * uint32_t(c), o);
       tmem_wait_ld();
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -794,7 +960,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
         const uint32_t h1 = pack_h2(__uint_as_float(o[8 * u + 2]) * inv_l, __uint_as_float(o[8 * u + 3]) * inv_l);
         const uint32_t h2 = pack_h2(__uint_as_float(o[8 * u + 4]) * inv_l, __uint_as_float(o[8 * u + 5]) * inv_l);
         const uint32_t h3 = pack_h2(__uint_as_float(o[8 * u + 6]) * inv_l, __uint_as_float(o[8 * u + 7]) * inv_l);
-        const int gu = c * 4 + u;  // 16-byte unit of the 256-byte output row
+        const int gu = 8 * grp + 4 * c + u;  // 16-byte unit of the 256-byte output row
         const uint32_t addr = sQ + uint32_t(gu >> 3) * kQHalfBytes + uint32_t(row) * 128 +
                               (uint32_t((gu & 7) ^ (row & 7)) << 4);
         st_shared_v4(addr, h0, h1, h2, h3);
@@ -802,26 +968,33 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
     }
     tc_fence_before();
     fence_proxy_async_smem();
-    mbar_arrive(sm.bar(kBarOStaged + t));
-    if (wq == 0 && lane == 0) {
+    arrive_local(kBarOStaged);
+    if (warp == 0 && lane == 0) {
       int bh, qb, cnt;
       plan_decode<int>(p.nqb, p.unit_begin, p.unit_end, item, bh, qb, cnt);
-      if (!w.wait(sm.bar(kBarOStaged + t), uint32_t(it) & 1u, site | (kBarOStaged + t))) {
+      const int orow = (qb + int(rank)) * kBlockM;
+      if (!w.wait(sm.bar(kBarOStaged), uint32_t(it) & 1u, site | kBarOStaged)) {
+        ok = false;
+      } else if (int(rank) < cnt &&
+                 !w.check(orow >= 0 && orow < p.nqb * kBlockM && bh >= 0 && bh < p.heads, site | (kCheckSite + 4u))) {
         ok = false;
       } else {
-        const int u = 2 * t + int(rank);
-        if (u < cnt) {
-          const int orow = (qb + u) * kBlockM;
+        if (int(rank) < cnt) {
           tma_store_3d(&p.tm_o, sQ, 0, orow, bh);
           tma_store_3d(&p.tm_o, sQ + kQHalfBytes, 64, orow, bh);
           bulk_commit_group();
           bulk_wait_group_read0();
         }
-        mbar_arrive(sm.bar(kBarQEmpty + t));
+        mbar_arrive(sm.bar(kBarQEmpty + qt));
       }
     }
+    // A failure seen by warp 0's storing lane ends the loop for its whole warp.
+    ok = __all_sync(0xffffffffu, ok);
   }
-  if (wq == 0 && lane == 0) bulk_wait_group0();
+  if (warp == 0 && lane == 0) bulk_wait_group0();
+  if constexpr (kDebug) {
+    if (wq == 0 && lane == 0) st_volatile_shared(sm.count_slot(4 + grp), blocks_done);
+  }
 }
 
 template <int kVariant, bool kCapture>
@@ -839,17 +1012,20 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
     for (int t = 0; t < 2; ++t) {
       mbar_init(sm.bar(kBarQFull + t), fed);
       mbar_init(sm.bar(kBarQEmpty + t), 1);
-      mbar_init(sm.bar(kBarPHalf + t), kTileWarps);
-      mbar_init(sm.bar(kBarPFull + t), kTileWarps);
-      mbar_init(sm.bar(kBarOStaged + t), 128);
-      mbar_init(sm.bar(kBarSLo + t), 1);
-      mbar_init(sm.bar(kBarSHi + t), 1);
-      mbar_init(sm.bar(kBarOFinal + t), 1);
+      mbar_init(sm.bar(kBarSFull + t), 1);
+      mbar_init(sm.bar(kBarSFree + t), kGroupWarps);
+      mbar_init(sm.bar(kBarPFull + t), kGroupWarps);
+      mbar_init(sm.bar(kBarPVDone + t), 1);
+      mbar_init(sm.bar(kBarRef + t), 4);
       mbar_init(sm.bar(kBarDrain + t), 1);
     }
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(sm.bar(kBarKVFull + s), fed);
-      mbar_init(sm.bar(kBarKVEmpty + s), 2);  // one release per tile
+    mbar_init(sm.bar(kBarXchg), 8);
+    mbar_init(sm.bar(kBarOStaged), 8);
+    for (int e = 0; e < kRing; ++e) {
+      mbar_init(sm.bar(kBarKFull + e), fed);
+      mbar_init(sm.bar(kBarKEmpty + e), 1);
+      mbar_init(sm.bar(kBarVFull + e), fed);
+      mbar_init(sm.bar(kBarVEmpty + e), 1);
     }
     st_volatile_shared(sm.abort_slot(), 0u);
     fence_mbarrier_init();
@@ -871,6 +1047,16 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
   tc_fence_after();
   const uint32_t tmem_base = ld_volatile_shared(sm.tmem_slot());
   const Waiter w{sm.abort_slot(), map_shared(sm.abort_slot(), rank ^ 1u), p.timeout_ns, p.ws};
+  if constexpr (kDebug) {
+    // The whole 512-column allocation starts at lane 0, column 0, and the
+    // aligned layout ends inside the dynamic shared memory.
+    if (threadIdx.x == 0) {
+      w.check(tmem_base == 0u && sm.base + uint32_t(kSmemUsed) <= raw + uint32_t(kSmemBytes),
+              (rank << 16) | (kCheckSite + 5u));
+      for (int r = 0; r < 6; ++r) st_volatile_shared(sm.count_slot(r), 0u);
+    }
+    __syncthreads();
+  }
 
   if (warp < 8) {
     regs_increase<kSoftmaxRegs>();
@@ -878,7 +1064,8 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
   } else {
     regs_decrease<kControlRegs>();
     if (lane == 0) {
-      if (rank == 0 && (warp == kMmaWarp || warp == kMmaWarp + 2)) mma_role(p, sm, tmem_base, w, int(warp - kMmaWarp) / 2);
+      if (rank == 0 && warp == kSIssuerWarp) s_issuer_role(p, sm, tmem_base, w);
+      else if (rank == 0 && warp == kPVIssuerWarp) pv_issuer_role(p, sm, tmem_base, w);
       else if (warp == kLoadWarp) load_role(p, sm, w, rank);
       else if (rank == 1 && warp == kForwardWarp) forward_role(p, sm, w);
     }
@@ -891,6 +1078,20 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+  if constexpr (kDebug) {
+    // Every role counted the same key blocks: the parity of every mbarrier
+    // wait derives from those counts.
+    if (threadIdx.x == 0 && ld_volatile_shared(sm.abort_slot()) == 0u) {
+      uint32_t items = 0;
+      for (int item = int(cluster_id_x()); item < p.num_items; item += int(num_clusters_x())) ++items;
+      const uint32_t want = items * uint32_t(p.n_kv);
+      const uint32_t groups = ld_volatile_shared(sm.count_slot(4)) + ld_volatile_shared(sm.count_slot(5));
+      bool same = ld_volatile_shared(sm.count_slot(2)) == want && groups == want;
+      if (rank == 0) same = same && ld_volatile_shared(sm.count_slot(0)) == want && ld_volatile_shared(sm.count_slot(1)) == want;
+      else same = same && ld_volatile_shared(sm.count_slot(3)) == want;
+      if (!same) w.fail((rank << 16) | (kCheckSite + 6u), kDevPhase);
+    }
   }
   if ((p.flags & kFlagTrace) && threadIdx.x == kLoadWarp * 32 && blockIdx.x < 1024) {
     uint32_t* rec = p.ws + (256 + 32 * blockIdx.x) / 4;

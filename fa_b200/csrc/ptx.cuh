@@ -203,77 +203,29 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// S = A * B^T for the pair (M = 256: 128 rows of A from each CTA's shared
-// memory; B's N rows split in half between the CTAs, same offsets in both)
-// over a 128-wide K as 8 K=16 steps in one asm block.  Both operands are
-// K-major with 128-byte swizzle in two 64-column halves kAHalf / kBHalf
-// apart (16-byte units).  Descriptors are passed as their low words (start
-// address in bits 0-13, 16-byte units) plus the common high word; step kk
-// adds (kk/4)*kXHalf + (kk%4)*2 (no carry: shared addresses are below
-// 256 KiB).  Step 0 overwrites D.
-template <uint32_t kAHalf, uint32_t kBHalf>
-__device__ __forceinline__ void mma_pair_ss_k128(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
-                                                 uint32_t idesc) {
+// One pair MMA (M = 256: 128 rows of A in each CTA; B's N rows split in
+// half between the CTAs, same shared-memory offsets in both), both operands
+// from shared memory, given by their 64-bit matrix descriptors.  acc = 0
+// overwrites D.  One instruction per asm statement: a thread issuing these
+// back to back keeps the tensor pipe busy at N = 128 (measured on B200:
+// ~60 cycles per issue against 64 of tensor work).
+__device__ __forceinline__ void mma_pair_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t acc) {
   asm volatile(
-      "{\n\t"
-      ".reg .b32 al, bl;\n\t"
-      ".reg .b64 da, db;\n\t"
-      ".reg .pred pf, pt;\n\t"
-      "setp.ne.b32 pf, %4, %4;\n\t"
-      "setp.eq.b32 pt, %4, %4;\n\t"
-      "mov.b64 da, {%1, %3};\n\t"
-      "mov.b64 db, {%2, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pf;\n\t"
-      "add.u32 al, %1, 2;\n\t add.u32 bl, %2, 2;\n\t"
-      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, 4;\n\t add.u32 bl, %2, 4;\n\t"
-      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, 6;\n\t add.u32 bl, %2, 6;\n\t"
-      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, %5;\n\t add.u32 bl, %2, %6;\n\t"
-      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, %7;\n\t add.u32 bl, %2, %8;\n\t"
-      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, %9;\n\t add.u32 bl, %2, %10;\n\t"
-      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "add.u32 al, %1, %11;\n\t add.u32 bl, %2, %12;\n\t"
-      "mov.b64 da, {al, %3};\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %4, pt;\n\t"
-      "}\n" ::"r"(d_tmem),
-      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "n"(kAHalf), "n"(kBHalf), "n"(kAHalf + 2), "n"(kBHalf + 2),
-      "n"(kAHalf + 4), "n"(kBHalf + 4), "n"(kAHalf + 6), "n"(kBHalf + 6)
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc)
       : "memory");
 }
 
-// O (+)= P * V for the pair over 64 keys as 4 K=16 steps: A = P from each
-// CTA's TMEM (8 columns per step), B = V (MN-major, this CTA's 64 head-dim
-// columns; 16 keys = 2 KiB per step).  first_acc = 0 overwrites O with the
-// first step.
-__device__ __forceinline__ void mma_pair_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi,
-                                                uint32_t idesc, uint32_t first_acc) {
+// The same with A from tensor memory (each CTA's 128 lanes hold its rows;
+// K = 16 FP16 values = 8 columns per instruction).
+__device__ __forceinline__ void mma_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t acc) {
   asm volatile(
-      "{\n\t"
-      ".reg .b32 ta, bl;\n\t"
-      ".reg .b64 db;\n\t"
-      ".reg .pred pf, pt;\n\t"
-      "setp.ne.b32 pf, %5, 0;\n\t"
-      "setp.eq.b32 pt, %4, %4;\n\t"
-      "mov.b64 db, {%2, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], db, %4, pf;\n\t"
-      "add.u32 ta, %1, 8;\n\t add.u32 bl, %2, 128;\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
-      "add.u32 ta, %1, 16;\n\t add.u32 bl, %2, 256;\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
-      "add.u32 ta, %1, 24;\n\t add.u32 bl, %2, 384;\n\t mov.b64 db, {bl, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
-      "}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(first_acc)
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc)
       : "memory");
 }
 
@@ -334,6 +286,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// MUFU base-2 exponential of two FP16 values (packed f16x2).
+__device__ __forceinline__ uint32_t ex2_approx_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
 
@@ -398,6 +357,22 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
                "r"(d)
                : "memory");
+}
+
+__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ float ld_volatile_global_f32(const float* p) {
+  float v;
+  asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ uint32_t ld_volatile_shared(uint32_t addr) {

@@ -34,7 +34,7 @@ WS_TRACE_BYTES = 32
 MAX_CTAS = 1024
 TIMELINE_BLOCKS = 48
 WS_TIMELINE_OFFSET = WS_HEADER_BYTES + WS_TRACE_BYTES * MAX_CTAS
-WS_TIMELINE_BYTES = 4 * TIMELINE_BLOCKS * 8 * 8
+WS_TIMELINE_BYTES = 2 * 4 * TIMELINE_BLOCKS * 8 * 8
 WS_BYTES = WS_TIMELINE_OFFSET + WS_TIMELINE_BYTES
 
 # name -> (restype, argtypes); the exported C ABI, one entry per declaration

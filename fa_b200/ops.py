@@ -113,7 +113,7 @@ class Operator:
         buffer, with the copies overlapped with the kernel.
 
         The unit range is cut into ``chunks`` contiguous pieces (whole work
-        items of four query blocks, the end pieces half-sized).  On an
+        items of two query blocks, the end pieces half-sized).  On an
         upload stream, each piece's K/V heads not yet on the device go up,
         then its Q rows; the piece's kernel runs on the current stream once
         they are there, and its O rows come down on a download stream while
@@ -231,12 +231,13 @@ class Operator:
             lib.reset_status(ws.data_ptr(), torch.cuda.current_stream(ws.device).cuda_stream)
 
     def timeline(self, device):
-        """CTA 0's clock64 stamps of the last B200FA_FLAG_TIMELINE call as an int64
-        tensor [4 roles, TIMELINE_BLOCKS, 8 events] (synchronizes)."""
+        """The first pair's clock64 stamps of the last B200FA_FLAG_TIMELINE call
+        as an int64 tensor [2 ranks, 4 roles, TIMELINE_BLOCKS, 8 events]
+        (synchronizes)."""
         ws = self.workspace(torch.device(device))
         torch.cuda.synchronize(ws.device)
         raw = ws[lib.WS_TIMELINE_OFFSET:lib.WS_TIMELINE_OFFSET + lib.WS_TIMELINE_BYTES]
-        return raw.view(torch.int64).view(4, lib.TIMELINE_BLOCKS, 8).cpu()
+        return raw.view(torch.int64).view(2, 4, lib.TIMELINE_BLOCKS, 8).cpu()
 
     def trace(self, device) -> list[dict]:
         """Per-CTA trace records of the last traced call (synchronizes).

@@ -44,7 +44,7 @@ def row_range(unit_begin: int, unit_end: int, Nq: int) -> tuple[int, int]:
     return unit_row(unit_begin, Nq), unit_row(unit_end, Nq)
 
 
-def pieces(unit_begin: int, unit_end: int, chunks: int, item_units: int = 4) -> list[int]:
+def pieces(unit_begin: int, unit_end: int, chunks: int, item_units: int = 2) -> list[int]:
     """Boundaries of ``chunks`` contiguous pieces of [unit_begin, unit_end)
     on whole work items (``item_units`` units from the range start), the
     first and last pieces half-sized when there are three or more: the

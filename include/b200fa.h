@@ -73,17 +73,22 @@ extern "C" {
 /* Device status word values (b200fa_read_status, status[0]). */
 #define B200FA_DEV_OK             0
 #define B200FA_DEV_TIMEOUT        1   /* a bounded mbarrier wait ran out       */
+/* Checking build only (libb200fa_debug.so, compiled with B200FA_DEBUG): */
+#define B200FA_DEV_BOUNDS         2   /* a coordinate, index or layout check failed;
+                                         site low byte = 0x80 + check number    */
+#define B200FA_DEV_PHASE          3   /* the roles' key-block counts disagreed at exit */
 
 /* Option flags (b200fa_options.flags). */
 #define B200FA_FLAG_TRACE          1u /* write one trace record per CTA        */
-/* Test-only: the softmax warps of query tile 1 (in both CTAs of every
- * pair) withhold their first P-ready arrival, so the MMA thread's bounded
+/* Test-only: softmax group 1 (the odd key blocks, in both CTAs of every
+ * pair) withholds its first P-ready arrival, so the PV issuer's bounded
  * wait runs out and the kernel reports B200FA_DEV_TIMEOUT.  Used by the
  * failure-detection test only. */
 #define B200FA_FLAG_TEST_WITHHOLD_P 2u
-/* Debug: CTA 0 records SM-clock timestamps of its softmax, MMA and TMA
- * threads for the first B200FA_TIMELINE_BLOCKS key blocks of its first work
- * item into the timeline area of the workspace (pipeline analysis). */
+/* Debug: both CTAs of the first pair record SM-clock timestamps of their
+ * softmax, MMA-issuer / forwarder and TMA threads for the first
+ * B200FA_TIMELINE_BLOCKS key blocks of their first work item into the
+ * timeline area of the workspace (pipeline analysis). */
 #define B200FA_FLAG_TIMELINE       4u
 /* Debug capture (the counterpart of the reference's `capture` attribute,
  * binding.py:39-41, vector_output.h:94-106): per key block and query row the
@@ -106,6 +111,11 @@ extern "C" {
  * capture serialises each block's softmax with its P V product: a debug
  * mode, not a fast path. */
 #define B200FA_FLAG_CAPTURE        8u
+/* Test-only, checking build only: the producer offsets its first Q tile's
+ * row coordinate past the end of the problem; the bounds check catches it
+ * before the copy is issued and the kernel reports B200FA_DEV_BOUNDS.  The
+ * product build ignores the flag (it has no checks and never offsets). */
+#define B200FA_FLAG_TEST_BOUNDS   16u
 #define B200FA_BLOCK_KEYS        128
 
 typedef struct b200fa_options {
@@ -131,15 +141,16 @@ typedef struct b200fa_options {
  *                  pair's items
  *   [B200FA_WS_TIMELINE_OFFSET, + B200FA_WS_TIMELINE_BYTES)
  *                  timeline (B200FA_FLAG_TIMELINE): u64 clock64 stamps,
- *                  [role 0..3][block 0..B200FA_TIMELINE_BLOCKS-1][event 0..7],
- *                  roles = softmax tile 0, softmax tile 1, MMA, TMA.
+ *                  [pair rank 0..1][role 0..3][block 0..B200FA_TIMELINE_BLOCKS-1]
+ *                  [event 0..7], roles = softmax group 0, softmax group 1,
+ *                  MMA issuers (rank 0) / forwarder (rank 1), TMA.
  * The status is sticky: it stays set until b200fa_reset_status. */
 #define B200FA_WS_HEADER_BYTES 256u
 #define B200FA_WS_TRACE_BYTES   32u
 #define B200FA_MAX_CTAS       1024
 #define B200FA_TIMELINE_BLOCKS  48u
 #define B200FA_WS_TIMELINE_OFFSET (B200FA_WS_HEADER_BYTES + B200FA_WS_TRACE_BYTES * B200FA_MAX_CTAS)
-#define B200FA_WS_TIMELINE_BYTES  (4u * B200FA_TIMELINE_BLOCKS * 8u * 8u)
+#define B200FA_WS_TIMELINE_BYTES  (2u * 4u * B200FA_TIMELINE_BLOCKS * 8u * 8u)
 
 /* Number of work units: (b, hq, 128-row query block) triples, linearised as
  * ((b * Hq) + hq) * ceil(Nq / 128) + qb -- the order of the reference's
@@ -192,8 +203,8 @@ int b200fa_reset_status(void* workspace, void* stream);
 const char* b200fa_kernel_name(int32_t variant);
 
 /* Host-side work-item plan (no GPU): item `index` of the range
- * [unit_begin, unit_end) as {bh, first q-block, count (1..4)}: up to four
- * consecutive query blocks of one head, processed by one CTA pair.  Returns
+ * [unit_begin, unit_end) as {bh, first q-block, count (1..2)}: up to two
+ * consecutive query blocks of one head, one per CTA of a pair.  Returns
  * the number of items, or a negative code. */
 int64_t b200fa_plan_item(int64_t B, int64_t Hq, int64_t Nq,
                          int64_t unit_begin, int64_t unit_end, int64_t index,

@@ -104,7 +104,7 @@ def test_work_plan_covers_every_unit_once(B, Hq, Nq):
             continue
         seen = []
         for bh, qb, cnt in lib.plan_items(B, Hq, Nq, ub, ue):
-            assert 1 <= cnt <= 4 and 0 <= qb and qb + cnt <= nqb
+            assert 1 <= cnt <= 2 and 0 <= qb and qb + cnt <= nqb
             seen.extend(bh * nqb + qb + i for i in range(cnt))
         assert seen == list(range(ub, ue))
 

@@ -133,7 +133,7 @@ def test_host_path_pieces(ub, ue, chunks):
     b = pieces(ub, ue, chunks)
     assert b[0] == ub and b[-1] == ue and all(x <= y for x, y in zip(b, b[1:]))
     assert 1 <= len(b) - 1 <= max(1, chunks)
-    assert all((x - ub) % 4 == 0 for x in b[:-1])
+    assert all((x - ub) % 2 == 0 for x in b[:-1])  # work items are two units
     sizes = [y - x for x, y in zip(b, b[1:])]
     if len(sizes) >= 3 and ue - ub >= 16 * chunks:
         assert max(sizes[0], sizes[-1]) <= min(sizes[1:-1])
