@@ -9,7 +9,11 @@ manifest of artifact hashes, no partial reuse), restated for nvcc.
 
 Runs on a CPU-only host: nvcc cross-compiles for sm_100a without a GPU.
 The library goes to ``fa_b200/_build/libb200fa.so`` (in-tree, git-ignored)
-so that it travels with the source tree to the GPU host.
+so that it travels with the source tree to the GPU host.  The checking
+build ``libb200fa_debug.so`` (``build(debug=True)``) is the same sources
+compiled with ``-DB200FA_DEBUG``: its kernels verify coordinates, indices
+and layout before use and the roles' key-block counts at exit, and report a
+violation in the device status word instead of touching memory.
 """
 
 from __future__ import annotations
@@ -31,6 +35,10 @@ BUILD_DIR = PKG_DIR / "_build"
 LIB_NAME = "libb200fa.so"
 LIB_PATH = BUILD_DIR / LIB_NAME
 MANIFEST = BUILD_DIR / "build.json"
+DEBUG_LIB_NAME = "libb200fa_debug.so"
+DEBUG_LIB_PATH = BUILD_DIR / DEBUG_LIB_NAME
+DEBUG_MANIFEST = BUILD_DIR / "build_debug.json"
+DEBUG_FLAGS = ["-DB200FA_DEBUG"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + [
@@ -56,7 +64,15 @@ def _nvcc_version(nvcc: str) -> str:
     return out.strip().splitlines()[-1]
 
 
-def source_identity(nvcc: str | None = None) -> str:
+def _flags(debug: bool) -> list[str]:
+    return NVCC_FLAGS + (DEBUG_FLAGS if debug else [])
+
+
+def _paths(debug: bool) -> tuple[Path, Path]:
+    return (DEBUG_LIB_PATH, DEBUG_MANIFEST) if debug else (LIB_PATH, MANIFEST)
+
+
+def source_identity(nvcc: str | None = None, debug: bool = False) -> str:
     nvcc = nvcc or nvcc_path()
     h = hashlib.sha256()
     for path in sorted(CSRC.glob("*")) + sorted(INCLUDE.glob("*.h")):
@@ -64,7 +80,7 @@ def source_identity(nvcc: str | None = None) -> str:
             h.update(path.name.encode())
             h.update(path.read_bytes())
     h.update(_nvcc_version(nvcc).encode())
-    h.update(" ".join(NVCC_FLAGS).encode())
+    h.update(" ".join(_flags(debug)).encode())
     return h.hexdigest()
 
 
@@ -72,46 +88,52 @@ def _file_hash(path: Path) -> str:
     return hashlib.sha256(path.read_bytes()).hexdigest()
 
 
-def is_current() -> bool:
+def is_current(debug: bool = False) -> bool:
     """True when the built library matches the current sources."""
-    if not LIB_PATH.is_file() or not MANIFEST.is_file():
+    lib_path, manifest_path = _paths(debug)
+    if not lib_path.is_file() or not manifest_path.is_file():
         return False
     try:
-        manifest = json.loads(MANIFEST.read_text())
-        return (manifest.get("identity") == source_identity()
-                and manifest.get("artifact_sha256") == _file_hash(LIB_PATH))
+        manifest = json.loads(manifest_path.read_text())
+        return (manifest.get("identity") == source_identity(debug=debug)
+                and manifest.get("artifact_sha256") == _file_hash(lib_path))
     except (OSError, ValueError, FileNotFoundError, subprocess.CalledProcessError):
         return False
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile ``libb200fa.so`` when the sources changed; return its path."""
+def build(force: bool = False, verbose: bool = False, debug: bool = False) -> Path:
+    """Compile ``libb200fa.so`` (``debug``: ``libb200fa_debug.so``) when the
+    sources changed; return its path."""
     BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    lib_path, manifest_path = _paths(debug)
+    flags = _flags(debug)
     with open(BUILD_DIR / ".lock", "a") as lock:
         fcntl.flock(lock, fcntl.LOCK_EX)
-        if not force and is_current():
-            return LIB_PATH
+        if not force and is_current(debug):
+            return lib_path
         nvcc = nvcc_path()
-        identity = source_identity(nvcc)
+        identity = source_identity(nvcc, debug)
         with tempfile.TemporaryDirectory(dir=BUILD_DIR) as tmp:
-            out = Path(tmp) / LIB_NAME
-            cmd = [nvcc, *NVCC_FLAGS, f"-I{INCLUDE}", "-o", str(out),
+            out = Path(tmp) / lib_path.name
+            cmd = [nvcc, *flags, f"-I{INCLUDE}", "-o", str(out),
                    *[str(CSRC / s) for s in SOURCES]]
             res = subprocess.run(cmd, capture_output=True, text=True)
-            (BUILD_DIR / "build.log").write_text(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+            log = BUILD_DIR / ("build_debug.log" if debug else "build.log")
+            log.write_text(" ".join(cmd) + "\n" + res.stdout + res.stderr)
             if res.returncode != 0:
                 raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stderr[-4000:]}")
             if verbose:
                 print(res.stderr)
-            os.replace(out, LIB_PATH)  # never leave a partial library behind
-        MANIFEST.write_text(json.dumps({
+            os.replace(out, lib_path)  # never leave a partial library behind
+        manifest_path.write_text(json.dumps({
             "identity": identity,
-            "artifact_sha256": _file_hash(LIB_PATH),
-            "flags": NVCC_FLAGS,
+            "artifact_sha256": _file_hash(lib_path),
+            "flags": flags,
             "sources": list(SOURCES),
         }, indent=2))
-        return LIB_PATH
+        return lib_path
 
 
 if __name__ == "__main__":
     print(build(force=True, verbose=True))
+    print(build(force=True, verbose=True, debug=True))

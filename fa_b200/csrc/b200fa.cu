@@ -23,9 +23,13 @@
 using namespace b200fa;
 
 static_assert(kTimelineOffset == B200FA_WS_TIMELINE_OFFSET, "timeline offset mismatch");
-static_assert(kTimelineBlocks == int(B200FA_TIMELINE_BLOCKS), "timeline size mismatch");
+static_assert(kTimelineBlocks == int(B200FA_TIMELINE_BLOCKS) && kTimelineRoles == int(B200FA_TIMELINE_ROLES),
+              "timeline size mismatch");
 static_assert(kBlockN == B200FA_BLOCK_KEYS, "capture block size mismatch");
 static_assert(kFlagCapture == B200FA_FLAG_CAPTURE, "capture flag mismatch");
+static_assert(kFlagTestBounds == B200FA_FLAG_TEST_BOUNDS, "test flag mismatch");
+static_assert(kDevTimeout == B200FA_DEV_TIMEOUT && kDevBounds == B200FA_DEV_BOUNDS && kDevPhase == B200FA_DEV_PHASE,
+              "device status codes mismatch");
 
 // Clusters of two CTAs: the pair that shares every tensor-core product.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)

@@ -140,7 +140,7 @@ constexpr int kSmemV = kSmemK + kRing * kStageBytes;
 constexpr int kSmemBar = kSmemV + kRing * kStageBytes;
 constexpr int kSmemXchg = kSmemBar + kNumBars * 8;        // float [2][128] reference / row-sum exchange
 constexpr int kSmemMisc = kSmemXchg + 2 * kBlockM * 4;    // TMEM base, abort flag, 6 block counters
-constexpr int kSmemUsed = kSmemMisc + 8 + 4 * 6;
+constexpr int kSmemUsed = kSmemMisc + 8 + 4 * 6 + 8;  // + start time (trace)
 constexpr int kSmemBytes = kSmemUsed + 1024;  // + slack for 1024-B alignment
 static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 static_assert(kSmemBar % 8 == 0, "mbarrier alignment");
@@ -261,13 +261,24 @@ constexpr uint32_t kCheckSite = 0x80u;  // low byte of a check's site: 0x80 + ch
 // Debug timeline (kFlagTimeline): both CTAs of the first pair stamp
 // clock64() at fixed points of their first work item's first kTimelineBlocks
 // key blocks.  Layout: u64 [rank][role][block][event] at byte
-// kTimelineOffset of the workspace; roles 0/1 = softmax group 0/1 (warp 4g;
-// each stamps its own blocks), 2 = rank 0's issuers / rank 1's forwarder,
-// 3 = TMA thread.  Softmax events: 0 scores ready seen, 1 scores loaded and
-// maximum reduced, 2 reference decided, 3 exponentials done, 4-7 P handed
-// over by the group's warps 0-3.  Issuer events: 0/1 PV started/issued, 2/3
-// S started/issued, 4 "S free" seen; forwarder events: 5/6 K/V forwarded.
-// TMA events: 0/1 K wait/issue, 2/3 V wait/issue.
+// kTimelineOffset of the workspace; roles 0-7 = softmax warps 0-7 (lane 0;
+// each group's warps stamp the group's blocks), 8 = rank 0's issuers / rank
+// 1's forwarder, 9 = TMA thread.  Softmax events: 0 block started (before
+// the reference wait), 1 reference and scores ready, 2 scores loaded and
+// maximum reduced, 3 reference published, 4 exponentials done, 5 P stored
+// in TMEM, 6 "P full" arrived, 7 reference seen.  Issuer events: 0/1 PV
+// started/issued, 2/3 S started/issued, 4 "S free" seen; rank 0's warp 11
+// (idle otherwise) watches the products complete: 5/6 "S full" / "PV done"
+// seen; forwarder events (rank 1): 5/6 K/V forwarded.  TMA events: 0/1 K
+// wait/issue, 2/3 V wait/issue.
+// The stamps are compiled into the checking build (and any build defining
+// B200FA_TIMELINE) only: the product kernels carry no timeline code.
+#if defined(B200FA_DEBUG) || defined(B200FA_TIMELINE)
+constexpr bool kTimeline = true;
+#else
+constexpr bool kTimeline = false;
+#endif
+constexpr int kTimelineRoles = 10;
 constexpr int kTimelineBlocks = 48;
 constexpr uint32_t kTimelineOffset = 256u + 32u * 1024u;
 
@@ -277,16 +288,16 @@ struct Timeline {
   const FwdParams* p;
   bool on;
   __device__ __forceinline__ void mark(int role, int j, int e) const {
-    if (on && j < kTimelineBlocks) {
+    if (kTimeline && on && j < kTimelineBlocks) {
       uint64_t* base = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(p->ws) + kTimelineOffset) +
-                       cluster_rank() * (4u * kTimelineBlocks * 8u);
+                       cluster_rank() * (uint32_t(kTimelineRoles) * kTimelineBlocks * 8u);
       base[(role * kTimelineBlocks + j) * 8 + e] = clock64();
     }
   }
 };
 
 __device__ __forceinline__ Timeline make_timeline(const FwdParams& p, int it, bool thread = true) {
-  return Timeline{&p, thread && (p.flags & kFlagTimeline) != 0 && cluster_id_x() == 0 && it == 0};
+  return Timeline{&p, kTimeline && thread && (p.flags & kFlagTimeline) != 0 && cluster_id_x() == 0 && it == 0};
 }
 
 template <typename I>
@@ -342,17 +353,15 @@ __host__ __device__ inline void plan_decode(I nqb, I ub, I ue, I x, I& bh, I& qb
 // Bounded mbarrier waits.  `site` identifies the wait in the status word:
 // (rank << 16) | (warp << 8) | barrier slot (or kCheckSite + check number).
 struct Waiter {
-  uint32_t abort_slot;       // shared u32, nonzero once any thread of the pair gave up
-  uint32_t peer_abort_slot;  // the other CTA's abort flag (cluster address)
-  uint64_t timeout_ns;
-  uint32_t* ws;
+  uint32_t abort_slot;   // shared u32, nonzero once any thread of the pair gave up
+  const FwdParams* p;    // the kernel parameters: bound, status words (read in place)
 
   __device__ __forceinline__ void fail(uint32_t site, uint32_t code = kDevTimeout) const {
     st_volatile_shared(abort_slot, 1u);
-    st_cluster_u32(peer_abort_slot, 1u);
-    if (atomicCAS(&ws[0], 0u, code) == 0u) {
-      ws[1] = site;
-      ws[2] = blockIdx.x;
+    st_cluster_u32(map_shared(abort_slot, cluster_rank() ^ 1u), 1u);  // the other CTA's flag
+    if (atomicCAS(&p->ws[0], 0u, code) == 0u) {
+      p->ws[1] = site;
+      p->ws[2] = blockIdx.x;
     }
     __threadfence();
   }
@@ -372,7 +381,7 @@ struct Waiter {
       for (int i = 0; i < 16; ++i)
         if (test<kCluster>(bar, parity)) return true;
       if (ld_volatile_shared(abort_slot) != 0u) return false;
-      if (global_timer_ns() - t0 > timeout_ns) {
+      if (global_timer_ns() - t0 > p->timeout_ns) {
         fail(site);
         return false;
       }
@@ -415,6 +424,8 @@ struct Smem {
   // Checking build: key blocks counted by role r (0 S issuer, 1 PV issuer,
   // 2 producer, 3 forwarder, 4/5 softmax group 0/1) at exit.
   __device__ __forceinline__ uint32_t count_slot(int r) const { return base + kSmemMisc + 8 + 4 * r; }
+  // Trace: the kernel's start time (two u32 words).
+  __device__ __forceinline__ uint32_t start_slot() const { return base + kSmemMisc + 32; }
 };
 
 // The CTA counts its key blocks over all its items: block g has its K in K
@@ -467,17 +478,17 @@ __device__ void s_issuer_role(const FwdParams& p, const Smem& sm, uint32_t tmem_
         ok = false;
         break;
       }
-      tl.mark(2, j, 4);
+      tl.mark(8, j, 4);
       if (!w.wait(sm.bar(kBarKFull + int(e)), ring_parity(g), site | uint32_t(kBarKFull + int(e)))) {
         ok = false;
         break;
       }
-      tl.mark(2, j, 2);
+      tl.mark(8, j, 2);
       tc_fence_after();
       issue_s(tmem_base + kTmemS + 128u * b, q_desc, smem_desc(sm.k(e)));
       mma_commit_pair_both(sm.bar(kBarSFull + int(b)));
       mma_commit_pair_both(sm.bar(kBarKEmpty + int(e)));
-      tl.mark(2, j, 3);
+      tl.mark(8, j, 3);
     }
   }
   if constexpr (kDebug) st_volatile_shared(sm.count_slot(0), g);
@@ -508,17 +519,40 @@ __device__ void pv_issuer_role(const FwdParams& p, const Smem& sm, uint32_t tmem
         ok = false;
         break;
       }
-      tl.mark(2, j, 0);
+      tl.mark(8, j, 0);
       tc_fence_after();
       issue_pv(tmem_base + kTmemO, tmem_base + kTmemP + 64u * b, smem_desc(sm.v(e)), j > 0 ? 1u : 0u);
       mma_commit_pair_both(sm.bar(kBarPVDone + int(b)));
       mma_commit_pair_both(sm.bar(kBarVEmpty + int(e)));
-      tl.mark(2, j, 1);
+      tl.mark(8, j, 1);
     }
   }
   if constexpr (kDebug) st_volatile_shared(sm.count_slot(1), g);
   mma_commit_pair(sm.bar(kBarDrain + 1));
   w.drain(sm.bar(kBarDrain + 1), 0u, 100000000ull);
+}
+
+// Timeline builds, rank 0's otherwise idle warp 11: stamps when each of the
+// first item's S and PV products completes (observes "S full" and "PV done"
+// in order).  Observation only: it gives up silently after the bound and
+// never records a status.
+__device__ void watch_role(const FwdParams& p, const Smem& sm) {
+  const Timeline tl = make_timeline(p, 0);
+  if (!tl.on || cluster_id_x() >= uint32_t(p.num_items)) return;
+  const int n = p.n_kv < kTimelineBlocks ? p.n_kv : kTimelineBlocks;
+  auto seen = [&](int bar, uint32_t parity) -> bool {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_test(sm.bar(bar), parity))
+      if (global_timer_ns() - t0 > p.timeout_ns) return false;
+    return true;
+  };
+  for (int j = 0; j < n; ++j) {
+    const uint32_t g = uint32_t(j);
+    if (!seen(kBarSFull + int(buf(g)), buf_parity(g))) return;
+    tl.mark(8, j, 5);
+    if (!seen(kBarPVDone + int(buf(g)), buf_parity(g))) return;
+    tl.mark(8, j, 6);
+  }
 }
 
 // Rank 1, one thread: replays the producer's sequence and, as each of this
@@ -545,9 +579,9 @@ __device__ void forward_role(const FwdParams& p, const Smem& sm, const Waiter& w
     for (int j = 0; j < n; ++j, ++g) {
       const int e = int(ring_entry(g));
       if (!forward(kBarKFull + e, ring_parity(g))) { ok = false; break; }
-      tl.mark(2, j, 5);
+      tl.mark(8, j, 5);
       if (!forward(kBarVFull + e, ring_parity(g))) { ok = false; break; }
-      tl.mark(2, j, 6);
+      tl.mark(8, j, 6);
     }
   }
   if constexpr (kDebug) st_volatile_shared(sm.count_slot(3), g);
@@ -598,9 +632,9 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, u
       const uint32_t ph = ring_parity(g);
       // K: keys [j*128 + 64r, +64), all 128 head-dim columns, as two 64-column
       // boxes, once S of block g - kRing completed.
-      tl.mark(3, j, 0);
+      tl.mark(9, j, 0);
       if (!w.wait(sm.bar(kBarKEmpty + int(e)), ph ^ 1u, site | (kBarKEmpty + e))) { ok = false; break; }
-      tl.mark(3, j, 1);
+      tl.mark(9, j, 1);
       const int krow = j * kBlockN + int(rank) * kKBoxRows;
       if (!w.check(krow >= 0 && krow + kKBoxRows <= key_end, site | (kCheckSite + 2u))) { ok = false; break; }
       mbar_arrive_expect_tx(sm.bar(kBarKFull + int(e)), kStageBytes);
@@ -610,9 +644,9 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, u
       last_par = (last_par & ~(1u << e)) | (ph << e);
       // V: keys [j*128, +128), head-dim columns [64r, +64), once PV of block
       // g - kRing completed.
-      tl.mark(3, j, 2);
+      tl.mark(9, j, 2);
       if (!w.wait(sm.bar(kBarVEmpty + int(e)), ph ^ 1u, site | (kBarVEmpty + e))) { ok = false; break; }
-      tl.mark(3, j, 3);
+      tl.mark(9, j, 3);
       if (!w.check(j * kBlockN + kBlockN <= key_end && int(rank) * kPairDims + kPairDims <= kHeadDim,
                    site | (kCheckSite + 3u))) {
         ok = false;
@@ -780,8 +814,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
     const uint32_t g0 = uint32_t(it) * uint32_t(n);  // the CTA's block count before this item
     float m_cur = -INFINITY;  // reference of this group's last block (log2 domain)
     float l_g = 0.f;          // this group's row sum over its blocks, relative to m_cur
-    const Timeline tl = make_timeline(p, it, wq == 0 && lane == 0);
-    const Timeline tl_warp = make_timeline(p, it, lane == 0);  // per-warp hand-off stamps
+    const Timeline tl = make_timeline(p, it, lane == 0);
     // Debug capture: cap_on (this CTA's unit exists in the item) is
     // warp-uniform, cap_row per thread (its query row exists).  Record
     // (b*Hq+hq, block j, row) sits at index (bh*n + j)*nq + row of each
@@ -831,6 +864,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       // first block (value unused): the wait orders this group's write of
       // slot gb % 2 after the other group's read of it.
       float m_prev = -INFINITY;
+      tl.mark(int(warp), j, 0);
       if (gb > 0) {
         if (!wait_warp(kBarRef + int((gb - 1u) & 1u), ((gb - 1u) >> 1) & 1u)) {
           ok = false;
@@ -838,18 +872,19 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
         }
         if (j > 0) m_prev = ld_shared_f32(sm.xchg((gb - 1u) & 1u, row));
       }
+      tl.mark(int(warp), j, 7);
       if (!wait_warp(kBarSFull + int(b), buf_parity(gb))) {
         ok = false;
         break;
       }
-      tl.mark(grp, j, 0);
+      tl.mark(int(warp), j, 1);
       tc_fence_after();
       const bool tail = (j == n - 1 && p.nk_tail < kBlockN);
       uint32_t r[kBlockN];
       load_scores(tS, r, tail, p.nk_tail);
       arrive_rank0(kBarSFree + int(b));  // the S issuer may refill the buffer
       const float mx = fmaxf(row_max64(r), row_max64(r + 64)) * sl2;
-      tl.mark(grp, j, 1);
+      tl.mark(int(warp), j, 2);
       // This group's partial sum follows the reference the other group left.
       if (j >= 2 && m_prev != m_cur) l_g *= ex2_approx(m_cur - m_prev);
       float m_new = m_prev, alpha = 1.f;
@@ -861,7 +896,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       }
       st_shared_f32(sm.xchg(gb & 1u, row), m_new);
       arrive_local(kBarRef + int(gb & 1u));
-      tl.mark(grp, j, 2);
+      tl.mark(int(warp), j, 3);
       if constexpr (kCapture) {
         if (cap_on && j > 0) {
           if (!wait_pv(gb - 1u)) { ok = false; break; }
@@ -877,7 +912,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       const uint64_t nm = f2_pack(-m_new, -m_new);
       exp_keys<kVariant, kPoly, 4>(r, sl2x2, nm, pk, acc0, acc1, hsum);
       exp_keys<kVariant, kPoly, 4>(r + 64, sl2x2, nm, pk + 32, acc0, acc1, hsum);
-      tl.mark(grp, j, 3);
+      tl.mark(int(warp), j, 4);
       if (__any_sync(0xffffffffu, moved)) {
         // Lazy correction of the running output before this block's P is
         // handed over: PV(gb-1) must be complete (PV(gb) waits for "P full").
@@ -911,10 +946,11 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       tmem_st32(tP, pk);
       tmem_st32(tP + 32u, pk + 32);
       tmem_wait_st();
+      tl.mark(int(warp), j, 5);
       tc_fence_before();
       if (!(withhold && it == 0 && j == 1)) arrive_rank0(kBarPFull + int(b));
       ++blocks_done;
-      tl_warp.mark(grp, j, 4 + wq);
+      tl.mark(int(warp), j, 6);
     }
     if (!ok) break;
 
@@ -997,17 +1033,20 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
   }
 }
 
-template <int kVariant, bool kCapture>
-__device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_addr(smem_raw);
-  Smem sm{(raw + 1023u) & ~1023u};
-  const uint32_t warp = threadIdx.x >> 5;
-  const uint32_t lane = threadIdx.x & 31u;
-  const uint32_t rank = cluster_rank();
-  const uint64_t t_start = global_timer_ns();
+__device__ __forceinline__ Smem smem_of(uint8_t* smem_raw) { return Smem{(smem_addr(smem_raw) + 1023u) & ~1023u}; }
 
-  if (threadIdx.x == 0) {
+__device__ __forceinline__ Waiter waiter_of(const FwdParams& p, const Smem& sm) { return Waiter{sm.abort_slot(), &p}; }
+
+// The kernel runs in three phases -- setup, roles, teardown -- that share no
+// register: what a later phase needs is read again from special registers
+// or shared memory.  Nothing is then live across the role split, where the
+// warpgroups' register counts differ (a value live there is spilled).
+__device__ __forceinline__ void setup_phase(const FwdParams& p, uint8_t* smem_raw) {
+  const Smem sm = smem_of(smem_raw);
+  const uint32_t tid = tid_x();
+  const uint32_t warp = tid >> 5, lane = tid & 31u;
+  const uint32_t rank = cluster_rank();
+  if (tid == 0) {
     const uint32_t fed = rank == 0 ? 2u : 1u;  // rank 0's full barriers also count rank 1's forward
     for (int t = 0; t < 2; ++t) {
       mbar_init(sm.bar(kBarQFull + t), fed);
@@ -1028,9 +1067,13 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
       mbar_init(sm.bar(kBarVEmpty + e), 1);
     }
     st_volatile_shared(sm.abort_slot(), 0u);
+    for (int r = 0; r < 6; ++r) st_volatile_shared(sm.count_slot(r), 0u);
     fence_mbarrier_init();
   }
   if (warp == kLoadWarp && lane == 0) {
+    const uint64_t t_start = global_timer_ns();
+    st_volatile_shared(sm.start_slot(), uint32_t(t_start));
+    st_volatile_shared(sm.start_slot() + 4, uint32_t(t_start >> 32));
     tma_prefetch_map(&p.tm_q);
     tma_prefetch_map(&p.tm_k);
     tma_prefetch_map(&p.tm_v);
@@ -1045,44 +1088,59 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
-  const uint32_t tmem_base = ld_volatile_shared(sm.tmem_slot());
-  const Waiter w{sm.abort_slot(), map_shared(sm.abort_slot(), rank ^ 1u), p.timeout_ns, p.ws};
   if constexpr (kDebug) {
     // The whole 512-column allocation starts at lane 0, column 0, and the
     // aligned layout ends inside the dynamic shared memory.
-    if (threadIdx.x == 0) {
-      w.check(tmem_base == 0u && sm.base + uint32_t(kSmemUsed) <= raw + uint32_t(kSmemBytes),
-              (rank << 16) | (kCheckSite + 5u));
-      for (int r = 0; r < 6; ++r) st_volatile_shared(sm.count_slot(r), 0u);
+    if (tid == 0) {
+      const uint32_t tmem_base = ld_volatile_shared(sm.tmem_slot());
+      waiter_of(p, sm).check(tmem_base == 0u && sm.base + uint32_t(kSmemUsed) <= smem_addr(smem_raw) + uint32_t(kSmemBytes),
+                             (rank << 16) | (kCheckSite + 5u));
     }
-    __syncthreads();
   }
+}
 
+template <int kVariant, bool kCapture>
+__device__ __forceinline__ void role_phase(const FwdParams& p, uint8_t* smem_raw) {
+  const Smem sm = smem_of(smem_raw);
+  const uint32_t tid = tid_x();
+  const uint32_t warp = tid >> 5, lane = tid & 31u;
   if (warp < 8) {
     regs_increase<kSoftmaxRegs>();
-    softmax_role<kVariant, kCapture>(p, sm, tmem_base, w, warp, lane, rank);
+    const uint32_t tmem_base = ld_volatile_shared(sm.tmem_slot());
+    softmax_role<kVariant, kCapture>(p, sm, tmem_base, waiter_of(p, sm), warp, lane, cluster_rank());
   } else {
     regs_decrease<kControlRegs>();
+    const uint32_t rank = cluster_rank();
     if (lane == 0) {
+      const uint32_t tmem_base = ld_volatile_shared(sm.tmem_slot());
+      const Waiter w = waiter_of(p, sm);
       if (rank == 0 && warp == kSIssuerWarp) s_issuer_role(p, sm, tmem_base, w);
       else if (rank == 0 && warp == kPVIssuerWarp) pv_issuer_role(p, sm, tmem_base, w);
       else if (warp == kLoadWarp) load_role(p, sm, w, rank);
       else if (rank == 1 && warp == kForwardWarp) forward_role(p, sm, w);
+      else if (kTimeline && rank == 0 && warp == kForwardWarp) watch_role(p, sm);
     }
   }
   __syncwarp();
+}
+
+__device__ __forceinline__ void teardown_phase(const FwdParams& p, uint8_t* smem_raw) {
+  const Smem sm = smem_of(smem_raw);
+  const uint32_t tid = tid_x();
+  const uint32_t warp = tid >> 5;
+  const uint32_t rank = cluster_rank();
   // Rank 0's MMAs read and write both CTAs' memories: neither CTA frees
   // TMEM or leaves before the pair is done.
   tc_fence_before();
   cluster_sync();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem_base, kTmemCols);
+    tmem_dealloc_pair(ld_volatile_shared(sm.tmem_slot()), kTmemCols);
   }
   if constexpr (kDebug) {
     // Every role counted the same key blocks: the parity of every mbarrier
     // wait derives from those counts.
-    if (threadIdx.x == 0 && ld_volatile_shared(sm.abort_slot()) == 0u) {
+    if (tid == 0 && ld_volatile_shared(sm.abort_slot()) == 0u) {
       uint32_t items = 0;
       for (int item = int(cluster_id_x()); item < p.num_items; item += int(num_clusters_x())) ++items;
       const uint32_t want = items * uint32_t(p.n_kv);
@@ -1090,23 +1148,31 @@ __device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
       bool same = ld_volatile_shared(sm.count_slot(2)) == want && groups == want;
       if (rank == 0) same = same && ld_volatile_shared(sm.count_slot(0)) == want && ld_volatile_shared(sm.count_slot(1)) == want;
       else same = same && ld_volatile_shared(sm.count_slot(3)) == want;
-      if (!same) w.fail((rank << 16) | (kCheckSite + 6u), kDevPhase);
+      if (!same) waiter_of(p, sm).fail((rank << 16) | (kCheckSite + 6u), kDevPhase);
     }
   }
-  if ((p.flags & kFlagTrace) && threadIdx.x == kLoadWarp * 32 && blockIdx.x < 1024) {
+  if ((p.flags & kFlagTrace) && tid == kLoadWarp * 32 && blockIdx.x < 1024) {
     uint32_t* rec = p.ws + (256 + 32 * blockIdx.x) / 4;
     int items = 0;
     for (int item = int(cluster_id_x()); item < p.num_items; item += int(num_clusters_x())) ++items;
     const uint64_t t_end = global_timer_ns();
     rec[0] = sm_id();
     rec[1] = uint32_t(items);
-    rec[2] = uint32_t(t_start);
-    rec[3] = uint32_t(t_start >> 32);
+    rec[2] = ld_volatile_shared(sm.start_slot());
+    rec[3] = ld_volatile_shared(sm.start_slot() + 4);
     rec[4] = uint32_t(t_end);
     rec[5] = uint32_t(t_end >> 32);
     rec[6] = rank;
     rec[7] = 0u;
   }
+}
+
+template <int kVariant, bool kCapture>
+__device__ __forceinline__ void attention_fwd_body(const FwdParams& p) {
+  extern __shared__ uint8_t smem_raw[];
+  setup_phase(p, smem_raw);
+  role_phase<kVariant, kCapture>(p, smem_raw);
+  teardown_phase(p, smem_raw);
 }
 
 }  // namespace b200fa

@@ -22,6 +22,14 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// %tid.x read by a volatile instruction: a value read again after a
+// register-count change is not kept live across it.
+__device__ __forceinline__ uint32_t tid_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%tid.x;" : "=r"(r));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t sm_id() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%smid;" : "=r"(r));

@@ -24,17 +24,22 @@ FLAG_TRACE = 1
 FLAG_TEST_WITHHOLD_P = 2
 FLAG_TIMELINE = 4
 FLAG_CAPTURE = 8
+FLAG_TEST_BOUNDS = 16
 BLOCK_KEYS = 128
 
 DEV_OK = 0
 DEV_TIMEOUT = 1
+DEV_BOUNDS = 2
+DEV_PHASE = 3
+CHECK_SITE = 0x80  # low byte of the status site of a failed check: 0x80 + check number
 
 WS_HEADER_BYTES = 256
 WS_TRACE_BYTES = 32
 MAX_CTAS = 1024
 TIMELINE_BLOCKS = 48
+TIMELINE_ROLES = 10
 WS_TIMELINE_OFFSET = WS_HEADER_BYTES + WS_TRACE_BYTES * MAX_CTAS
-WS_TIMELINE_BYTES = 2 * 4 * TIMELINE_BLOCKS * 8 * 8
+WS_TIMELINE_BYTES = 2 * TIMELINE_ROLES * TIMELINE_BLOCKS * 8 * 8
 WS_BYTES = WS_TIMELINE_OFFSET + WS_TIMELINE_BYTES
 
 # name -> (restype, argtypes); the exported C ABI, one entry per declaration
@@ -70,7 +75,7 @@ SIGNATURES = {
 }
 
 _lock = threading.Lock()
-_lib = None
+_libs: dict[bool, C.CDLL] = {}  # debug -> bound library
 
 
 class B200FAError(RuntimeError):
@@ -81,34 +86,35 @@ class B200FAError(RuntimeError):
         self.status = status
 
 
-def load(build_if_needed: bool = True) -> C.CDLL:
-    """Load (building first if the sources changed) and bind the library."""
-    global _lib
+def load(build_if_needed: bool = True, debug: bool = False) -> C.CDLL:
+    """Load (building first if the sources changed) and bind the library;
+    ``debug`` selects the checking build libb200fa_debug.so."""
     with _lock:
-        if _lib is not None:
-            return _lib
+        lib = _libs.get(debug)
+        if lib is not None:
+            return lib
         if build_if_needed:
-            path = _build.build()
+            path = _build.build(debug=debug)
         else:
-            path = _build.LIB_PATH
+            path = _build.DEBUG_LIB_PATH if debug else _build.LIB_PATH
             if not path.is_file():
-                raise FileNotFoundError(f"{path} is not built; run fa_b200.build.build()")
+                raise FileNotFoundError(f"{path} is not built; run fa_b200.build.build(debug={debug})")
         lib = C.CDLL(str(path), mode=C.RTLD_LOCAL)
         for name, (restype, argtypes) in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        _lib = lib
+        _libs[debug] = lib
         return lib
 
 
-def last_error() -> str:
-    return load().b200fa_last_error_string().decode()
+def last_error(debug: bool = False) -> str:
+    return load(debug=debug).b200fa_last_error_string().decode()
 
 
-def check(status: int, where: str) -> None:
+def check(status: int, where: str, debug: bool = False) -> None:
     if status != 0:
-        raise B200FAError(where, status, last_error())
+        raise B200FAError(where, status, last_error(debug))
 
 
 def num_units(B: int, Hq: int, Nq: int) -> int:
@@ -154,12 +160,13 @@ def kernel_name(variant: int) -> str:
 
 def fwd(q_ptr, k_ptr, v_ptr, o_ptr, B, Hq, Hkv, Nq, Nk, D, scale, variant,
         unit_begin, unit_end, ws_ptr, ws_bytes, stream, *, flags=0, timeout_us=0, max_ctas=0,
-        capture_ptr=None, capture_bytes=0):
-    """Raw pointer call of b200fa_fwd_ex; raises B200FAError on a nonzero status."""
+        capture_ptr=None, capture_bytes=0, debug=False):
+    """Raw pointer call of b200fa_fwd_ex (``debug``: of the checking build);
+    raises B200FAError on a nonzero status."""
     opts = Options(C.sizeof(Options), flags, timeout_us, max_ctas, capture_ptr, capture_bytes)
-    status = load().b200fa_fwd_ex(q_ptr, k_ptr, v_ptr, o_ptr, B, Hq, Hkv, Nq, Nk, D, scale, variant,
-                                  unit_begin, unit_end, ws_ptr, ws_bytes, stream, C.byref(opts))
-    check(status, "b200fa_fwd")
+    status = load(debug=debug).b200fa_fwd_ex(q_ptr, k_ptr, v_ptr, o_ptr, B, Hq, Hkv, Nq, Nk, D, scale, variant,
+                                             unit_begin, unit_end, ws_ptr, ws_bytes, stream, C.byref(opts))
+    check(status, "b200fa_fwd", debug)
 
 
 def capture_bytes(B, Hq, Nq, Nk) -> int:

@@ -50,10 +50,14 @@ class Operator:
 
     variant: "fp16" (row sums over the FP16 P in FP16 partial sums, after the
              CCE FP16 kernel) or "fp32" (FP32 softmax, the CCE FP32 kernel).
+    debug:   run the checking build (libb200fa_debug.so): same results, plus
+             bounds, index and layout checks before every copy and a check of
+             the roles' key-block counts at exit, reported as
+             B200FA_DEV_BOUNDS / B200FA_DEV_PHASE in ``status``.
     """
 
     def __init__(self, variant: str = "fp16", *, timeout_us: int = 0, trace: bool = False,
-                 max_ctas: int = 0):
+                 max_ctas: int = 0, debug: bool = False):
         if variant not in lib.VARIANTS:
             raise ValueError(f"variant must be one of {sorted(lib.VARIANTS)}")
         self.variant = variant
@@ -61,9 +65,10 @@ class Operator:
         self.timeout_us = int(timeout_us)
         self.flags = lib.FLAG_TRACE if trace else 0
         self.max_ctas = int(max_ctas)
+        self.debug = bool(debug)
         self.workspaces = {}  # device -> uint8 tensor (zeroed once)
         self._streams = {}    # device -> (upload, download) streams of forward_host
-        lib.load()
+        lib.load(debug=self.debug)
 
     @property
     def kernel_name(self) -> str:
@@ -103,7 +108,7 @@ class Operator:
                     B, Hq, Hkv, Nq, Nk, HEAD_DIM, scale, self.variant_id, begin, end,
                     ws.data_ptr(), ws.numel(), stream,
                     flags=self.flags | flags | cap_flag, timeout_us=self.timeout_us, max_ctas=self.max_ctas,
-                    capture_ptr=cap_ptr, capture_bytes=cap_bytes)
+                    capture_ptr=cap_ptr, capture_bytes=cap_bytes, debug=self.debug)
         return out
 
     def forward_host(self, q_host, k_host, v_host, out_host, *, q_dev, k_dev, v_dev, o_dev,
@@ -232,12 +237,12 @@ class Operator:
 
     def timeline(self, device):
         """The first pair's clock64 stamps of the last B200FA_FLAG_TIMELINE call
-        as an int64 tensor [2 ranks, 4 roles, TIMELINE_BLOCKS, 8 events]
+        as an int64 tensor [2 ranks, TIMELINE_ROLES, TIMELINE_BLOCKS, 8 events]
         (synchronizes)."""
         ws = self.workspace(torch.device(device))
         torch.cuda.synchronize(ws.device)
         raw = ws[lib.WS_TIMELINE_OFFSET:lib.WS_TIMELINE_OFFSET + lib.WS_TIMELINE_BYTES]
-        return raw.view(torch.int64).view(2, 4, lib.TIMELINE_BLOCKS, 8).cpu()
+        return raw.view(torch.int64).view(2, lib.TIMELINE_ROLES, lib.TIMELINE_BLOCKS, 8).cpu()
 
     def trace(self, device) -> list[dict]:
         """Per-CTA trace records of the last traced call (synchronizes).

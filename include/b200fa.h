@@ -85,7 +85,8 @@ extern "C" {
  * wait runs out and the kernel reports B200FA_DEV_TIMEOUT.  Used by the
  * failure-detection test only. */
 #define B200FA_FLAG_TEST_WITHHOLD_P 2u
-/* Debug: both CTAs of the first pair record SM-clock timestamps of their
+/* Debug, checking build only (libb200fa_debug.so; the product build ignores
+ * the flag): both CTAs of the first pair record SM-clock timestamps of their
  * softmax, MMA-issuer / forwarder and TMA threads for the first
  * B200FA_TIMELINE_BLOCKS key blocks of their first work item into the
  * timeline area of the workspace (pipeline analysis). */
@@ -141,16 +142,18 @@ typedef struct b200fa_options {
  *                  pair's items
  *   [B200FA_WS_TIMELINE_OFFSET, + B200FA_WS_TIMELINE_BYTES)
  *                  timeline (B200FA_FLAG_TIMELINE): u64 clock64 stamps,
- *                  [pair rank 0..1][role 0..3][block 0..B200FA_TIMELINE_BLOCKS-1]
- *                  [event 0..7], roles = softmax group 0, softmax group 1,
- *                  MMA issuers (rank 0) / forwarder (rank 1), TMA.
+ *                  [pair rank 0..1][role 0..B200FA_TIMELINE_ROLES-1]
+ *                  [block 0..B200FA_TIMELINE_BLOCKS-1][event 0..7], roles =
+ *                  softmax warps 0-7, MMA issuers (rank 0) / forwarder
+ *                  (rank 1), TMA.
  * The status is sticky: it stays set until b200fa_reset_status. */
 #define B200FA_WS_HEADER_BYTES 256u
 #define B200FA_WS_TRACE_BYTES   32u
 #define B200FA_MAX_CTAS       1024
 #define B200FA_TIMELINE_BLOCKS  48u
+#define B200FA_TIMELINE_ROLES   10u
 #define B200FA_WS_TIMELINE_OFFSET (B200FA_WS_HEADER_BYTES + B200FA_WS_TRACE_BYTES * B200FA_MAX_CTAS)
-#define B200FA_WS_TIMELINE_BYTES  (2u * 4u * B200FA_TIMELINE_BLOCKS * 8u * 8u)
+#define B200FA_WS_TIMELINE_BYTES  (2u * B200FA_TIMELINE_ROLES * B200FA_TIMELINE_BLOCKS * 8u * 8u)
 
 /* Number of work units: (b, hq, 128-row query block) triples, linearised as
  * ((b * Hq) + hq) * ceil(Nq / 128) + qb -- the order of the reference's
