@@ -101,11 +101,14 @@ constexpr int kLoadWarp = 9;
 constexpr int kPVIssuerWarp = 10;  // rank 0: issues every PV product
 constexpr int kForwardWarp = 11;   // rank 1
 // Register split (setmaxnreg): launch 384 x 168 = 64512; softmax warpgroups
-// 256 x 192 + warpgroup 2 128 x 120 = 64512.  ptxas holds each region to its
-// share, so the control roles' 64-bit descriptors need the 120.
+// 256 x 208 + warpgroup 2 128 x 88 = 64512.  ptxas holds each region to its
+// share (both build flavours compile spill-free at this split).
+#ifndef B200FA_SOFTMAX_REGS
+#define B200FA_SOFTMAX_REGS 208
+#endif
 constexpr uint32_t kLaunchRegs = 168;
-constexpr uint32_t kSoftmaxRegs = 192;
-constexpr uint32_t kControlRegs = 120;
+constexpr uint32_t kSoftmaxRegs = B200FA_SOFTMAX_REGS;
+constexpr uint32_t kControlRegs = (kThreads * kLaunchRegs - 256 * kSoftmaxRegs) / 128 / 8 * 8;
 static_assert(256 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs, "register split exceeds the launch budget");
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (factor 256)
 
@@ -187,13 +190,6 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
 #endif
 template <int kVariant>
 constexpr int kPolyPairsOf = kVariant == 0 ? B200FA_POLY_PAIRS_FP16 : B200FA_POLY_PAIRS_FP32;
-// FP16 variant: MUFU exponentials of FP16 arguments in packed pairs (the
-// reference FP16 kernel's exp in FP16) instead of FP32 exponentials rounded
-// to FP16 (compile-time option).
-#ifndef B200FA_FP16_EXP_HALF2
-#define B200FA_FP16_EXP_HALF2 0
-#endif
-constexpr bool kExpHalf2 = B200FA_FP16_EXP_HALF2 != 0;
 constexpr float kExp2C0 = 0.9999280571937561f;
 constexpr float kExp2C1 = 0.6932609677314758f;
 constexpr float kExp2C2 = 0.2426111251115799f;
@@ -263,10 +259,10 @@ constexpr uint32_t kCheckSite = 0x80u;  // low byte of a check's site: 0x80 + ch
 // key blocks.  Layout: u64 [rank][role][block][event] at byte
 // kTimelineOffset of the workspace; roles 0-7 = softmax warps 0-7 (lane 0;
 // each group's warps stamp the group's blocks), 8 = rank 0's issuers / rank
-// 1's forwarder, 9 = TMA thread.  Softmax events: 0 block started (before
-// the reference wait), 1 reference and scores ready, 2 scores loaded and
+// 1's forwarder, 9 = TMA thread.  Softmax events: 0 block started, 7 scores
+// ready, 1 their loads issued and the reference seen, 2 scores loaded and
 // maximum reduced, 3 reference published, 4 exponentials done, 5 P stored
-// in TMEM, 6 "P full" arrived, 7 reference seen.  Issuer events: 0/1 PV
+// in TMEM, 6 "P full" arrived.  Issuer events: 0/1 PV
 // started/issued, 2/3 S started/issued, 4 "S free" seen; rank 0's warp 11
 // (idle otherwise) watches the products complete: 5/6 "S full" / "PV done"
 // seen; forwarder events (rank 1): 5/6 K/V forwarded.  TMA events: 0/1 K
@@ -532,26 +528,23 @@ __device__ void pv_issuer_role(const FwdParams& p, const Smem& sm, uint32_t tmem
   w.drain(sm.bar(kBarDrain + 1), 0u, 100000000ull);
 }
 
-// Timeline builds, rank 0's otherwise idle warp 11: stamps when each of the
-// first item's S and PV products completes (observes "S full" and "PV done"
-// in order).  Observation only: it gives up silently after the bound and
-// never records a status.
-__device__ void watch_role(const FwdParams& p, const Smem& sm) {
+// Timeline builds, rank 0's otherwise idle warp 11: lane 0 stamps when
+// each of the first item's S products completes ("S full"), lane 1 each PV
+// product ("PV done").  A buffer's next phase needs the softmax to have
+// consumed this one, so a watcher polling without pause sees every phase.
+// Observation only: it gives up silently after the bound and never records
+// a status.
+__device__ void watch_role(const FwdParams& p, const Smem& sm, uint32_t lane) {
   const Timeline tl = make_timeline(p, 0);
-  if (!tl.on || cluster_id_x() >= uint32_t(p.num_items)) return;
+  if (!tl.on || cluster_id_x() >= uint32_t(p.num_items) || lane > 1) return;
   const int n = p.n_kv < kTimelineBlocks ? p.n_kv : kTimelineBlocks;
-  auto seen = [&](int bar, uint32_t parity) -> bool {
-    const uint64_t t0 = global_timer_ns();
-    while (!mbar_test(sm.bar(bar), parity))
-      if (global_timer_ns() - t0 > p.timeout_ns) return false;
-    return true;
-  };
+  const int bar0 = lane == 0 ? kBarSFull : kBarPVDone;
   for (int j = 0; j < n; ++j) {
     const uint32_t g = uint32_t(j);
-    if (!seen(kBarSFull + int(buf(g)), buf_parity(g))) return;
-    tl.mark(8, j, 5);
-    if (!seen(kBarPVDone + int(buf(g)), buf_parity(g))) return;
-    tl.mark(8, j, 6);
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_test(sm.bar(bar0 + int(buf(g))), buf_parity(g)))
+      if (global_timer_ns() - t0 > p.timeout_ns) return;
+    tl.mark(8, j, 5 + int(lane));
   }
 }
 
@@ -674,8 +667,7 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, u
 // Exponentials of 16*kGroups keys (8 pairs per group) of one row:
 // x = s * scale*log2(e) - m with packed FP32 FMAs; of every 8 pairs the last
 // kPoly go through the FMA-pipe polynomial (exp2_poly2) and the rest through
-// MUFU (FP32 ex2, or for the FP16 variant with kExpHalf2 FP16 ex2 of the
-// packed pair).  Writes 8*kGroups packed FP16 pairs of P and adds the row
+// MUFU (FP32 ex2).  Writes 8*kGroups packed FP16 pairs of P and adds the row
 // sum: FP32 variant, the FP32 exponentials into packed FP32 sums (four
 // chains, folded into acc0/acc1); FP16 variant, the FP16 P itself into
 // packed FP16 sums (four chains; at most 16*kGroups <= 64 terms of <= 2^8,
@@ -692,24 +684,18 @@ __device__ __forceinline__ void exp_keys(const uint32_t* r, uint64_t sl2x2, uint
     for (int pp = 0; pp < 8; ++pp) {
       const int i = g * 8 + pp;  // key pair index
       const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sl2x2, nmx2);
-      if (kVariant == 0 && kExpHalf2 && pp < 8 - kPoly) {
+      uint64_t p2;
+      if (pp >= 8 - kPoly) {
+        p2 = exp2_poly2(x2);
+      } else {
         float a, b;
         f2_unpack(x2, a, b);
-        pk[i] = ex2_approx_h2(pack_h2(a, b));
-      } else {
-        uint64_t p2;
-        if (pp >= 8 - kPoly) {
-          p2 = exp2_poly2(x2);
-        } else {
-          float a, b;
-          f2_unpack(x2, a, b);
-          p2 = f2_pack(ex2_approx(a), ex2_approx(b));
-        }
-        float ea, eb;
-        f2_unpack(p2, ea, eb);
-        pk[i] = pack_h2(ea, eb);
-        if constexpr (kVariant == 1) cacc[pp & 3] = f2_add(cacc[pp & 3], p2);
+        p2 = f2_pack(ex2_approx(a), ex2_approx(b));
       }
+      float ea, eb;
+      f2_unpack(p2, ea, eb);
+      pk[i] = pack_h2(ea, eb);
+      if constexpr (kVariant == 1) cacc[pp & 3] = f2_add(cacc[pp & 3], p2);
       if constexpr (kVariant == 0) hc[pp & 3] = (g == 0 && pp < 4) ? pk[i] : hadd2(hc[pp & 3], pk[i]);
     }
   }
@@ -739,20 +725,6 @@ __device__ __forceinline__ void mask_keys64(uint32_t* r, int first, int valid) {
 #pragma unroll
   for (int i = 0; i < 64; ++i)
     if (first + i >= valid) r[i] = __float_as_uint(-INFINITY);
-}
-
-// Scores of a block's 128 keys of this thread's row from TMEM; keys at or
-// beyond `valid` (the last block's key count) get score -inf.
-__device__ __forceinline__ void load_scores(uint32_t tS, uint32_t* r, bool tail, int valid) {
-  tmem_ld32(tS, r);
-  tmem_ld32(tS + 32u, r + 32);
-  tmem_ld32(tS + 64u, r + 64);
-  tmem_ld32(tS + 96u, r + 96);
-  tmem_wait_ld();
-  if (tail) {
-    mask_keys64(r, 0, valid);
-    mask_keys64(r + 64, 64, valid);
-  }
 }
 
 // O row of this thread (128 FP32 columns in TMEM) times `f`, in place.
@@ -859,29 +831,38 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       const uint32_t b = buf(gb);
       const uint32_t tS = tmem_base + lane_off + kTmemS + 128u * b;
       const uint32_t tP = tmem_base + lane_off + kTmemP + 64u * b;
-      // Reference after block j-1 ("ref" gb-1, published by the other group
-      // about one block period earlier).  Waited for also at an item's
-      // first block (value unused): the wait orders this group's write of
-      // slot gb % 2 after the other group's read of it.
       float m_prev = -INFINITY;
       tl.mark(int(warp), j, 0);
+      if (!wait_warp(kBarSFull + int(b), buf_parity(gb))) {
+        ok = false;
+        break;
+      }
+      tl.mark(int(warp), j, 7);
+      tc_fence_after();
+      const bool tail = (j == n - 1 && p.nk_tail < kBlockN);
+      uint32_t r[kBlockN];
+      tmem_ld32(tS, r);
+      tmem_ld32(tS + 32u, r + 32);
+      tmem_ld32(tS + 64u, r + 64);
+      tmem_ld32(tS + 96u, r + 96);
+      // While the scores are on their way: the reference after block j-1
+      // ("ref" gb-1, published by the other group).  Waited for also at an
+      // item's first block (value unused): the wait orders this group's
+      // write of slot gb % 2 after the other group's read of it.
       if (gb > 0) {
         if (!wait_warp(kBarRef + int((gb - 1u) & 1u), ((gb - 1u) >> 1) & 1u)) {
+          tmem_wait_ld();
           ok = false;
           break;
         }
         if (j > 0) m_prev = ld_shared_f32(sm.xchg((gb - 1u) & 1u, row));
       }
-      tl.mark(int(warp), j, 7);
-      if (!wait_warp(kBarSFull + int(b), buf_parity(gb))) {
-        ok = false;
-        break;
-      }
       tl.mark(int(warp), j, 1);
-      tc_fence_after();
-      const bool tail = (j == n - 1 && p.nk_tail < kBlockN);
-      uint32_t r[kBlockN];
-      load_scores(tS, r, tail, p.nk_tail);
+      tmem_wait_ld();
+      if (tail) {
+        mask_keys64(r, 0, p.nk_tail);
+        mask_keys64(r + 64, 64, p.nk_tail);
+      }
       arrive_rank0(kBarSFree + int(b));  // the S issuer may refill the buffer
       const float mx = fmaxf(row_max64(r), row_max64(r + 64)) * sl2;
       tl.mark(int(warp), j, 2);
@@ -1118,8 +1099,8 @@ __device__ __forceinline__ void role_phase(const FwdParams& p, uint8_t* smem_raw
       else if (rank == 0 && warp == kPVIssuerWarp) pv_issuer_role(p, sm, tmem_base, w);
       else if (warp == kLoadWarp) load_role(p, sm, w, rank);
       else if (rank == 1 && warp == kForwardWarp) forward_role(p, sm, w);
-      else if (kTimeline && rank == 0 && warp == kForwardWarp) watch_role(p, sm);
     }
+    if (kTimeline && rank == 0 && warp == kForwardWarp) watch_role(p, sm, lane);
   }
   __syncwarp();
 }
