@@ -183,7 +183,7 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
 // Of every 8 key pairs, these go to the polynomial (a compile-time tuning
 // parameter per variant).
 #ifndef B200FA_POLY_PAIRS_FP16
-#define B200FA_POLY_PAIRS_FP16 2
+#define B200FA_POLY_PAIRS_FP16 1
 #endif
 #ifndef B200FA_POLY_PAIRS_FP32
 #define B200FA_POLY_PAIRS_FP32 1
@@ -672,7 +672,18 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, u
 // chains, folded into acc0/acc1); FP16 variant, the FP16 P itself into
 // packed FP16 sums (four chains; at most 16*kGroups <= 64 terms of <= 2^8,
 // far inside FP16 range), carried over to FP32 once per call (hsum).
-template <int kVariant, int kPoly, int kGroups>
+// FP16 row sum of 64 keys' P (32 packed pairs): four packed-FP16 chains,
+// folded and carried over to FP32.
+__device__ __forceinline__ float fp16_row_sum64(const uint32_t* pk) {
+  uint32_t hc[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) hc[c] = pk[c];
+#pragma unroll
+  for (int i = 4; i < 32; ++i) hc[i & 3] = hadd2(hc[i & 3], pk[i]);
+  return h2_sum_f32(hadd2(hadd2(hc[0], hc[1]), hadd2(hc[2], hc[3])));
+}
+
+template <int kVariant, int kPoly, int kGroups, bool kSum = true>
 __device__ __forceinline__ void exp_keys(const uint32_t* r, uint64_t sl2x2, uint64_t nmx2, uint32_t* pk,
                                          uint64_t& acc0, uint64_t& acc1, float& hsum) {
   static_assert(kGroups <= 4, "FP16 partial sums cover at most 64 keys");
@@ -696,10 +707,10 @@ __device__ __forceinline__ void exp_keys(const uint32_t* r, uint64_t sl2x2, uint
       f2_unpack(p2, ea, eb);
       pk[i] = pack_h2(ea, eb);
       if constexpr (kVariant == 1) cacc[pp & 3] = f2_add(cacc[pp & 3], p2);
-      if constexpr (kVariant == 0) hc[pp & 3] = (g == 0 && pp < 4) ? pk[i] : hadd2(hc[pp & 3], pk[i]);
+      if constexpr (kVariant == 0 && kSum) hc[pp & 3] = (g == 0 && pp < 4) ? pk[i] : hadd2(hc[pp & 3], pk[i]);
     }
   }
-  if constexpr (kVariant == 0) hsum += h2_sum_f32(hadd2(hadd2(hc[0], hc[1]), hadd2(hc[2], hc[3])));
+  if constexpr (kVariant == 0 && kSum) hsum += h2_sum_f32(hadd2(hadd2(hc[0], hc[1]), hadd2(hc[2], hc[3])));
   if constexpr (kVariant == 1) {
     acc0 = f2_add(acc0, f2_add(cacc[0], cacc[2]));
     acc1 = f2_add(acc1, f2_add(cacc[1], cacc[3]));
@@ -891,8 +902,12 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       uint64_t acc0 = 0ull, acc1 = 0ull;  // packed FP32 partial row sums
       float hsum = 0.f;                   // FP16 variant: sums of FP16 group sums
       const uint64_t nm = f2_pack(-m_new, -m_new);
-      exp_keys<kVariant, kPoly, 4>(r, sl2x2, nm, pk, acc0, acc1, hsum);
-      exp_keys<kVariant, kPoly, 4>(r + 64, sl2x2, nm, pk + 32, acc0, acc1, hsum);
+      // FP16 variant: the row sum of the FP16 P is taken after P has been
+      // handed over (its conversions then long complete, and off the
+      // hand-off path); the capture kernels need it earlier.
+      constexpr bool kLateSum = kVariant == 0 && !kCapture;
+      exp_keys<kVariant, kPoly, 4, !kLateSum>(r, sl2x2, nm, pk, acc0, acc1, hsum);
+      exp_keys<kVariant, kPoly, 4, !kLateSum>(r + 64, sl2x2, nm, pk + 32, acc0, acc1, hsum);
       tl.mark(int(warp), j, 4);
       if (__any_sync(0xffffffffu, moved)) {
         // Lazy correction of the running output before this block's P is
@@ -905,7 +920,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       f2_unpack(acc0, a0, b0);
       f2_unpack(acc1, a1, b1);
       const float z = ((a0 + b0) + (a1 + b1)) + hsum;
-      l_g += z;
+      if constexpr (!kLateSum) l_g += z;
       if constexpr (kCapture) {
         // Running row sum over both groups: the other group's record of
         // block j-1 holds the total after it; it was written and fenced
@@ -930,6 +945,7 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       tl.mark(int(warp), j, 5);
       tc_fence_before();
       if (!(withhold && it == 0 && j == 1)) arrive_rank0(kBarPFull + int(b));
+      if constexpr (kLateSum) l_g += fp16_row_sum64(pk) + fp16_row_sum64(pk + 32);
       ++blocks_done;
       tl.mark(int(warp), j, 6);
     }
