@@ -140,3 +140,36 @@ def test_capture_size_and_validation_without_gpu():
     legacy = lib.Options(16, 0, 0, 0, None, 0)
     assert lib.load().b200fa_fwd_ex(16, 16, 16, 16, 1, 2, 1, 300, 1000, 128, 0.088, 0, 2, 2,
                                     256, 1 << 20, None, C.byref(legacy)) == 0
+
+
+def test_python_constants_match_the_header():
+    """fa_b200/lib.py restates the header's #defines (flags, status codes,
+    workspace layout): they must agree, or a Python caller would pass the
+    wrong bits."""
+    import re
+    from pathlib import Path
+
+    text = (Path(__file__).resolve().parents[1] / "include" / "b200fa.h").read_text()
+    defs = dict(re.findall(r"#define\s+(B200FA_\w+)\s+([0-9]+)u?\b", text))
+    pairs = {
+        "B200FA_FLAG_TRACE": lib.FLAG_TRACE,
+        "B200FA_FLAG_TEST_WITHHOLD_P": lib.FLAG_TEST_WITHHOLD_P,
+        "B200FA_FLAG_TIMELINE": lib.FLAG_TIMELINE,
+        "B200FA_FLAG_CAPTURE": lib.FLAG_CAPTURE,
+        "B200FA_FLAG_TEST_BOUNDS": lib.FLAG_TEST_BOUNDS,
+        "B200FA_BLOCK_KEYS": lib.BLOCK_KEYS,
+        "B200FA_DEV_OK": lib.DEV_OK,
+        "B200FA_DEV_TIMEOUT": lib.DEV_TIMEOUT,
+        "B200FA_DEV_BOUNDS": lib.DEV_BOUNDS,
+        "B200FA_DEV_PHASE": lib.DEV_PHASE,
+        "B200FA_WS_HEADER_BYTES": lib.WS_HEADER_BYTES,
+        "B200FA_WS_TRACE_BYTES": lib.WS_TRACE_BYTES,
+        "B200FA_MAX_CTAS": lib.MAX_CTAS,
+        "B200FA_TIMELINE_BLOCKS": lib.TIMELINE_BLOCKS,
+        "B200FA_TIMELINE_ROLES": lib.TIMELINE_ROLES,
+        "B200FA_VARIANT_FP16": lib.VARIANT_FP16,
+        "B200FA_VARIANT_FP32": lib.VARIANT_FP32,
+    }
+    for name, value in pairs.items():
+        assert int(defs[name]) == value, name
+    assert lib.WS_TIMELINE_BYTES == 2 * lib.TIMELINE_ROLES * lib.TIMELINE_BLOCKS * 8 * 8
