@@ -86,3 +86,52 @@ def test_planted_bad_coordinate_is_caught_not_issued(variant):
     torch.cuda.synchronize(dev)
     assert dbg.status(dev)[0] == lib.DEV_OK and prod.status(dev)[0] == lib.DEV_OK
     assert torch.equal(out, ref)
+
+
+@pytest.mark.gpu
+def test_timeline_records_every_role_in_pipeline_order():
+    """B200FA_FLAG_TIMELINE (checking build): both CTAs of the first pair
+    stamp clock64 at fixed points of their first item's first blocks.  Each
+    softmax warp stamps its group's blocks in program order, the issuers,
+    the forwarder and the producer theirs; the product build ignores the
+    flag and leaves the area untouched."""
+    import numpy as np
+    import torch
+
+    from fa_b200.ops import Operator
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(9)
+    q = torch.randn((1, 12, 8192, 128), device=dev, generator=g).half()
+    k = torch.randn((1, 1, 8192, 128), device=dev, generator=g).half()
+    v = torch.randn((1, 1, 8192, 128), device=dev, generator=g).half()
+    dbg = Operator("fp32", debug=True)
+    dbg.workspace(dev).zero_()
+    dbg(q, k, v, flags=lib.FLAG_TIMELINE)
+    assert dbg.status(dev)[0] == lib.DEV_OK
+    t = dbg.timeline(dev).numpy()
+    assert t.shape == (2, lib.TIMELINE_ROLES, lib.TIMELINE_BLOCKS, 8)
+    n = min(8192 // 128, lib.TIMELINE_BLOCKS)
+    order = [0, 7, 1, 2, 3, 4, 5, 6]  # start, scores ready, ref seen, max, published, exps, P stored, P arrived
+    for rank in (0, 1):
+        for w in range(8):
+            for j in range(n):
+                e = t[rank, w, j]
+                if j % 2 == w // 4:
+                    assert np.all(e[order] > 0) and np.all(np.diff(e[order]) >= 0), (rank, w, j, e)
+                else:
+                    assert np.all(e == 0), (rank, w, j, e)
+        tma = t[rank, 9, :n]
+        assert np.all(tma[:, :4] > 0) and np.all(np.diff(tma[:, :4], axis=1) >= 0)
+    iss = t[0, 8, :n]
+    assert np.all(iss[:, 2] <= iss[:, 3]) and np.all(iss[:, 0] <= iss[:, 1])  # S / PV: started before issued
+    assert np.all(iss[2:, 4] <= iss[2:, 2])  # S of block j waits for "S free" of block j-2
+    assert np.all(iss[:, 5] > 0) and np.all(iss[:, 6] > 0)  # completions watched
+    fwd = t[1, 8, :n]
+    assert np.all(fwd[:, 5] > 0) and np.all(fwd[:, 5] <= fwd[:, 6])  # K forwarded, then V
+
+    prod = Operator("fp32")
+    prod.workspace(dev).zero_()
+    prod(q, k, v, flags=lib.FLAG_TIMELINE)
+    assert prod.status(dev)[0] == lib.DEV_OK
+    assert not prod.timeline(dev).any()
