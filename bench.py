@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--variant fp16|fp32]
                     [--impl b200|reference] [--shape B,Hq,Hkv,N]
 
-Workload: the BASELINE metric's configuration, B=2, Hq=12, Hkv=1,
+Workload: the headline metric's configuration, B=2, Hq=12, Hkv=1,
 Nq=Nk=131072, D=128 (reference problem/cases.py CASES[0]), Q/K/V i.i.d.
 N(0,1) FP16 drawn on the device from seed 0 (synthetic, canonical.py
 semantics).  One step = one attention forward over the whole case; with N
@@ -67,7 +67,7 @@ def parse_args():
     p.add_argument("--variant", choices=("fp16", "fp32"), default="fp16")
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--shape", type=str, default="2,12,1,131072",
-                   help="B,Hq,Hkv,N (default: the BASELINE metric config)")
+                   help="B,Hq,Hkv,N (default: the headline metric config)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-chunks", type=int, default=4,
                    help="pieces of the unit range whose copies overlap the kernel in the e2e leg")

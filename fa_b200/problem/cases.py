@@ -6,7 +6,7 @@ logical workload (B, S, Hq, Hkv, D) of one non-causal GQA forward over full
 and the name ``B{b}_S{s}_Q{hq}_KV{hkv}_D{d}``.
 
 ``CASES`` keeps the reference's three cases at indices 0-2 (same meaning as
-in the reference) and appends the two additional BASELINE configurations:
+in the reference) and appends the two additional benchmark configurations:
 (B=1, S=2048, Hq=12, Hkv=1) and (B=4, S=8192, Hq=32, Hkv=8).
 """
 
@@ -40,11 +40,11 @@ class Case:
 
 
 CASES = (
-    Case(2, 131072, 12, 1, 128),   # reference index 0 (BASELINE C5, headline)
+    Case(2, 131072, 12, 1, 128),   # reference index 0 (C5, the headline configuration)
     Case(2, 65536, 12, 1, 128),    # reference index 1 (C4)
     Case(1, 32768, 12, 1, 128),    # reference index 2 (C3)
-    Case(1, 2048, 12, 1, 128),     # BASELINE C1: plumbing case, CPU-checkable in full
-    Case(4, 8192, 32, 8, 128),     # BASELINE C2: 4:1 grouping
+    Case(1, 2048, 12, 1, 128),     # C1: plumbing case, CPU-checkable in full
+    Case(4, 8192, 32, 8, 128),     # C2: 4:1 grouping
 )
 
 HEADLINE = CASES[0]

@@ -14,7 +14,7 @@ It executes three pieces of the reference and records their results:
    its own with ``torch`` as its only global.  Its outputs (FP16 O) for
    seeded small inputs go to ``attention_vectors.npz``.
 2. ``Case`` and ``CASES`` (problem/cases.py:13-39): names, scale and group
-   size of the reference's cases plus the BASELINE configurations go to
+   size of the reference's cases plus the added benchmark configurations go to
    ``cases.json``.
 3. ``build_canonical`` (problem/canonical.py:18-28), run with the NPU device
    redirected to the CPU, on small cases: a checksum of its q/k/v goes to

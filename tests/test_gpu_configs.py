@@ -1,4 +1,4 @@
-"""GPU parity at the BASELINE configurations, against the FP32 oracle run on
+"""GPU parity at the benchmark configurations, against the FP32 oracle run on
 the GPU (TF32 off) on the same seeded canonical inputs.
 
 * C2 (4,32,8,8192) and C3 (1,12,1,32768): every element of O.
@@ -9,7 +9,7 @@ the GPU (TF32 off) on the same seeded canonical inputs.
 * C1 (1,12,1,2048) runs in full in tests/test_gpu_parity.py.
 
 The cases are the reference's own (problem/cases.py:35-39) plus the two
-configurations BASELINE adds; inputs follow problem/canonical.py:18-28
+configurations the benchmark adds; inputs follow problem/canonical.py:18-28
 (seed 0, q then k then v, N(0,1) FP16) on the GPU's RNG stream.  Bar: max-abs
 <= 2e-3 and mean-abs <= 2e-4 on O, both variants.
 """

@@ -5,7 +5,7 @@ same inputs, max-abs error <= 2e-3 and mean-abs error <= 2e-4 on O, for both
 variants.  Shapes cover the reference's edge cases and the relaxations of
 this build: GQA groupings (G = 1, 2, 4, 12), query/key tails (N % 128 != 0),
 Nq != Nk, a single key block, a single query block per head (lone work
-items), large-magnitude inputs, and the BASELINE plumbing case C1 in full.
+items), large-magnitude inputs, and the plumbing case C1 in full.
 """
 
 import pytest

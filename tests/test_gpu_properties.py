@@ -1,4 +1,4 @@
-"""Size-independent properties of the GPU path, up to the full BASELINE sizes.
+"""Size-independent properties of the GPU path, up to the full benchmark sizes.
 
 * shard consistency: running the unit grid as N contiguous shards (the
   multi-GPU split, emulated on one GPU) gives O bit-identical to one call,
