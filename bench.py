@@ -69,7 +69,7 @@ def parse_args():
     p.add_argument("--shape", type=str, default="2,12,1,131072",
                    help="B,Hq,Hkv,N (default: the headline metric config)")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--e2e-chunks", type=int, default=4,
+    p.add_argument("--e2e-chunks", type=int, default=3,
                    help="pieces of the unit range whose copies overlap the kernel in the e2e leg")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-verify", action="store_true",

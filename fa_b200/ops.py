@@ -113,12 +113,12 @@ class Operator:
 
     def forward_host(self, q_host, k_host, v_host, out_host, *, q_dev, k_dev, v_dev, o_dev,
                      scale: float | None = None, unit_range: tuple[int, int] | None = None,
-                     chunks: int = 4) -> tuple[int, int]:
+                     chunks: int = 3) -> tuple[int, int]:
         """O = attention(Q, K, V) from pinned host buffers into a pinned host
         buffer, with the copies overlapped with the kernel.
 
         The unit range is cut into ``chunks`` contiguous pieces (whole work
-        items of two query blocks, the end pieces half-sized).  On an
+        items of two query blocks, the end pieces quarter-sized).  On an
         upload stream, each piece's K/V heads not yet on the device go up,
         then its Q rows; the piece's kernel runs on the current stream once
         they are there, and its O rows come down on a download stream while

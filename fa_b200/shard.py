@@ -47,7 +47,7 @@ def row_range(unit_begin: int, unit_end: int, Nq: int) -> tuple[int, int]:
 def pieces(unit_begin: int, unit_end: int, chunks: int, item_units: int = 2) -> list[int]:
     """Boundaries of ``chunks`` contiguous pieces of [unit_begin, unit_end)
     on whole work items (``item_units`` units from the range start), the
-    first and last pieces half-sized when there are three or more: the
+    first and last pieces quarter-sized when there are three or more: the
     schedule of ``Operator.forward_host``, whose end pieces' copies are the
     ones not hidden behind a kernel.  Returns n+1 increasing boundaries
     from unit_begin to unit_end (n >= 1; pieces may be empty only when the
@@ -58,7 +58,7 @@ def pieces(unit_begin: int, unit_end: int, chunks: int, item_units: int = 2) -> 
     n = max(1, min(int(chunks), items))
     w = [1.0] * n
     if n >= 3:
-        w[0] = w[-1] = 0.5
+        w[0] = w[-1] = 0.25
     acc = [0.0]
     for x in w:
         acc.append(acc[-1] + x)
