@@ -27,13 +27,19 @@ SHAPES = [
     (1, 8, 2, 1000, 777),
     (2, 8, 2, 384, 1024),
     (1, 12, 1, 2048, 2048),
-    # tails on the 128-key block's parts (32 keys per CTA per 64-key half):
-    # 1 key, exactly one part (32), one half (64), three parts (96)
+    # tails of the last 128-key block (rank r of a CTA pair holds its keys
+    # [64r, 64r+64)): 1 key, 32, exactly one CTA's half (64), 96
     (1, 2, 1, 1, 1),
     (1, 2, 1, 129, 129),
     (1, 4, 1, 160, 160),
     (1, 2, 1, 300, 192),
     (1, 2, 2, 64, 224),
+    # several work items per CTA pair, so the two softmax groups' block parity
+    # flips at item boundaries (odd block counts) or one group has no block
+    # at all (a single block per item)
+    (1, 16, 1, 4096, 384),
+    (2, 32, 4, 1024, 640),
+    (1, 64, 8, 512, 100),
 ]
 
 
