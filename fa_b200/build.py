@@ -49,7 +49,7 @@ NVCC_FLAGS = ARCH_FLAGS + [
     "-shared",
     "-Xptxas", "-v",
 ]
-SOURCES = ("b200fa.cu",)
+SOURCES = ("b200fa.cu", "b200fa_causal.cu")
 
 
 def nvcc_path() -> str:

@@ -28,6 +28,7 @@ static_assert(kTimelineBlocks == int(B200FA_TIMELINE_BLOCKS) && kTimelineRoles =
 static_assert(kBlockN == B200FA_BLOCK_KEYS, "capture block size mismatch");
 static_assert(kFlagCapture == B200FA_FLAG_CAPTURE, "capture flag mismatch");
 static_assert(kFlagTestBounds == B200FA_FLAG_TEST_BOUNDS, "test flag mismatch");
+static_assert(kFlagCausal == B200FA_FLAG_CAUSAL, "causal flag mismatch");
 static_assert(kDevTimeout == B200FA_DEV_TIMEOUT && kDevBounds == B200FA_DEV_BOUNDS && kDevPhase == B200FA_DEV_PHASE,
               "device status codes mismatch");
 
@@ -53,6 +54,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   attention_fwd_body<1, true>(p);
 }
 
+// Causal-mask kernels, defined in b200fa_causal.cu (B200FA_FLAG_CAUSAL).
+__global__ void b200_fa_fp16_causal_kernel(const __grid_constant__ FwdParams p);
+__global__ void b200_fa_fp32_causal_kernel(const __grid_constant__ FwdParams p);
+
 // Test hook (b200fa_test_exp2): the softmax's two exponential forms on an
 // array, pairwise as the softmax evaluates them -- exp2_poly2 (FMA pipe) into
 // `poly`, MUFU ex2.approx into `mufu`.
@@ -73,8 +78,9 @@ __global__ void __launch_bounds__(256) exp2_probe_kernel(const float* x, float* 
 
 using KernelFn = void (*)(FwdParams);
 
-KernelFn kernel_for(int variant, bool capture) {
+KernelFn kernel_for(int variant, bool capture, bool causal) {
   if (capture) return variant == B200FA_VARIANT_FP16 ? b200_fa_fp16_capture_kernel : b200_fa_fp32_capture_kernel;
+  if (causal) return variant == B200FA_VARIANT_FP16 ? b200_fa_fp16_causal_kernel : b200_fa_fp32_causal_kernel;
   return variant == B200FA_VARIANT_FP16 ? b200_fa_fp16_kernel : b200_fa_fp32_kernel;
 }
 
@@ -125,10 +131,10 @@ int device_setup(int dev, int* pairs) {
   std::call_once(d.once, [&d] {
     cudaError_t e = cudaSuccess;
     for (int variant : {B200FA_VARIANT_FP16, B200FA_VARIANT_FP32})
-      for (bool capture : {false, true})
+      for (int kind = 0; kind < 3; ++kind)  // product, capture, causal
         if (e == cudaSuccess)
-          e = cudaFuncSetAttribute(kernel_for(variant, capture), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   kSmemBytes);
+          e = cudaFuncSetAttribute(kernel_for(variant, kind == 1, kind == 2),
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cudaLaunchAttribute attr[1];
@@ -218,6 +224,8 @@ int64_t capture_bytes(int64_t B, int64_t Hq, int64_t Nq, int64_t Nk) {
 // Capture buffer checks (B200FA_FLAG_CAPTURE).
 int check_capture(const b200fa_options& o, int64_t B, int64_t Hq, int64_t Nq, int64_t Nk) {
   if ((o.flags & B200FA_FLAG_CAPTURE) == 0) return B200FA_OK;
+  if (o.flags & B200FA_FLAG_CAUSAL)
+    return fail(B200FA_ERR_OPTIONS, "B200FA_FLAG_CAPTURE is not supported together with B200FA_FLAG_CAUSAL");
   const uint64_t need = uint64_t(capture_bytes(B, Hq, Nq, Nk));
   if (o.capture == nullptr || (reinterpret_cast<uintptr_t>(o.capture) & 15u) != 0 || o.capture_bytes < need)
     return fail(B200FA_ERR_OPTIONS, "B200FA_FLAG_CAPTURE needs a 16-byte aligned buffer of at least %llu bytes",
@@ -288,7 +296,8 @@ int fill_params(const void* q, const void* k, const void* v, void* o, int64_t B,
 }
 
 int launch(int32_t variant, const FwdParams& p, int grid, void* stream, const char* where) {
-  kernel_for(variant, p.capture != nullptr)<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(p);
+  kernel_for(variant, p.capture != nullptr, (p.flags & kFlagCausal) != 0)<<<grid, kThreads, kSmemBytes,
+                                                                          static_cast<cudaStream_t>(stream)>>>(p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, where);
   return B200FA_OK;

@@ -80,6 +80,16 @@
 #include <cuda.h>
 #include "ptx.cuh"
 
+// B200FA_CAUSAL = 1: this translation unit's kernels apply the causal mask
+// (query row i attends keys 0..i).  The causal kernels are compiled in their
+// own translation unit (b200fa_causal.cu), so that the product kernels are
+// compiled from exactly the non-causal source: the pipeline's timing is
+// sensitive to the instruction schedule, and folding the option into one
+// source moved the product kernels by 2 % (A/B on one box).
+#ifndef B200FA_CAUSAL
+#define B200FA_CAUSAL 0
+#endif
+
 namespace b200fa {
 
 constexpr int kBlockM = 128;    // query rows per unit (per CTA)
@@ -240,6 +250,7 @@ constexpr uint32_t kFlagTestWithholdP = 2u;
 constexpr uint32_t kFlagTimeline = 4u;
 constexpr uint32_t kFlagCapture = 8u;
 constexpr uint32_t kFlagTestBounds = 16u;  // checking build: one planted out-of-range coordinate
+constexpr uint32_t kFlagCausal = 32u;      // causal mask (kernels of the causal translation unit)
 
 // Checking build (B200FA_DEBUG): coordinates, indices and layout are
 // verified before use and the roles' block counts at exit; a violation is
@@ -345,6 +356,17 @@ __host__ __device__ inline void plan_decode(I nqb, I ub, I ue, I x, I& bh, I& qb
   const I left = ue - h1 * nqb - qb;
   cnt = left < G ? left : G;
 }
+
+#if B200FA_CAUSAL
+// Key blocks of work item `item` with the causal mask: up to the diagonal
+// block of the item's last unit.  Every role derives its block count, and
+// with it every barrier parity, from this function.
+__device__ __forceinline__ int item_blocks_causal(const FwdParams& p, int item) {
+  int bh, qb, cnt;
+  plan_decode<int>(p.nqb, p.unit_begin, p.unit_end, item, bh, qb, cnt);
+  return qb + cnt < p.n_kv ? qb + cnt : p.n_kv;
+}
+#endif
 
 // Bounded mbarrier waits.  `site` identifies the wait in the status word:
 // (rank << 16) | (warp << 8) | barrier slot (or kCheckSite + check number).
@@ -464,6 +486,9 @@ __device__ void s_issuer_role(const FwdParams& p, const Smem& sm, uint32_t tmem_
   uint32_t g = 0;  // the CTA's key blocks so far
   bool ok = true;
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
+#if B200FA_CAUSAL
+    const int n = item_blocks_causal(p, item);  // this item's blocks
+#endif
     const Timeline tl = make_timeline(p, it);
     const int qt = it & 1;
     const uint64_t q_desc = smem_desc(sm.q(qt));
@@ -504,6 +529,9 @@ __device__ void pv_issuer_role(const FwdParams& p, const Smem& sm, uint32_t tmem
   uint32_t g = 0;
   bool ok = true;
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
+#if B200FA_CAUSAL
+    const int n = item_blocks_causal(p, item);  // this item's blocks
+#endif
     const Timeline tl = make_timeline(p, it);
     for (int j = 0; j < n; ++j, ++g) {
       const uint32_t b = buf(g), e = ring_entry(g);
@@ -537,7 +565,12 @@ __device__ void pv_issuer_role(const FwdParams& p, const Smem& sm, uint32_t tmem
 __device__ void watch_role(const FwdParams& p, const Smem& sm, uint32_t lane) {
   const Timeline tl = make_timeline(p, 0);
   if (!tl.on || cluster_id_x() >= uint32_t(p.num_items) || lane > 1) return;
+#if B200FA_CAUSAL
+  const int n0 = item_blocks_causal(p, int(cluster_id_x()));
+  const int n = n0 < kTimelineBlocks ? n0 : kTimelineBlocks;
+#else
   const int n = p.n_kv < kTimelineBlocks ? p.n_kv : kTimelineBlocks;
+#endif
   const int bar0 = lane == 0 ? kBarSFull : kBarPVDone;
   for (int j = 0; j < n; ++j) {
     const uint32_t g = uint32_t(j);
@@ -567,6 +600,9 @@ __device__ void forward_role(const FwdParams& p, const Smem& sm, const Waiter& w
   };
   bool ok = true;
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
+#if B200FA_CAUSAL
+    const int n = item_blocks_causal(p, item);  // this item's blocks
+#endif
     const Timeline tl = make_timeline(p, it);
     if (!forward(kBarQFull + (it & 1), uint32_t(it >> 1) & 1u)) break;
     for (int j = 0; j < n; ++j, ++g) {
@@ -593,6 +629,9 @@ __device__ void load_role(const FwdParams& p, const Smem& sm, const Waiter& w, u
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
     int bh, qb, cnt;
     plan_decode<int>(p.nqb, p.unit_begin, p.unit_end, item, bh, qb, cnt);
+#if B200FA_CAUSAL
+    const int n = qb + cnt < p.n_kv ? qb + cnt : p.n_kv;  // this item's blocks (item_blocks_causal)
+#endif
     const int b = bh / p.Hq;
     const int kvh = b * p.Hkv + (bh - b * p.Hq) / p.group;
     // Rank r holds unit r of the item; a one-unit item repeats it in rank 1
@@ -792,9 +831,26 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
   };
   bool ok = true;
   uint32_t blocks_done = 0;  // checking build: this group's key blocks
+#if B200FA_CAUSAL
+  uint32_t g_items = 0;      // the CTA's key blocks of all earlier items
+#endif
 
   for (int item = int(cluster_id_x()), it = 0; ok && item < p.num_items; item += int(num_clusters_x()), ++it) {
+#if B200FA_CAUSAL
+    const int n = item_blocks_causal(p, item);  // this item's blocks
+    const uint32_t g0 = g_items;                // the CTA's block count before this item
+    g_items += uint32_t(n);
+    // This thread's query row (rank r holds unit r of the item; a one-unit
+    // item repeats it in rank 1): the mask's bound.
+    int qrow_g;
+    {
+      int bh_i, qb_i, cnt_i;
+      plan_decode<int>(p.nqb, p.unit_begin, p.unit_end, item, bh_i, qb_i, cnt_i);
+      qrow_g = (qb_i + (int(rank) < cnt_i ? int(rank) : cnt_i - 1)) * kBlockM + row;
+    }
+#else
     const uint32_t g0 = uint32_t(it) * uint32_t(n);  // the CTA's block count before this item
+#endif
     float m_cur = -INFINITY;  // reference of this group's last block (log2 domain)
     float l_g = 0.f;          // this group's row sum over its blocks, relative to m_cur
     const Timeline tl = make_timeline(p, it, lane == 0);
@@ -850,7 +906,15 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       }
       tl.mark(int(warp), j, 7);
       tc_fence_after();
+#if B200FA_CAUSAL
+      // Valid keys of the block for this row: the last block's key count
+      // and the keys up to the row.
+      int valid = j == p.n_kv - 1 ? p.nk_tail : kBlockN;
+      if (qrow_g - j * kBlockN + 1 < valid) valid = qrow_g - j * kBlockN + 1;
+      const bool tail = valid < kBlockN;
+#else
       const bool tail = (j == n - 1 && p.nk_tail < kBlockN);
+#endif
       uint32_t r[kBlockN];
       tmem_ld32(tS, r);
       tmem_ld32(tS + 32u, r + 32);
@@ -871,8 +935,13 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       tl.mark(int(warp), j, 1);
       tmem_wait_ld();
       if (tail) {
+#if B200FA_CAUSAL
+        mask_keys64(r, 0, valid);
+        mask_keys64(r + 64, 64, valid);
+#else
         mask_keys64(r, 0, p.nk_tail);
         mask_keys64(r + 64, 64, p.nk_tail);
+#endif
       }
       arrive_rank0(kBarSFree + int(b));  // the S issuer may refill the buffer
       const float mx = fmaxf(row_max64(r), row_max64(r + 64)) * sl2;
@@ -1140,7 +1209,14 @@ __device__ __forceinline__ void teardown_phase(const FwdParams& p, uint8_t* smem
     if (tid == 0 && ld_volatile_shared(sm.abort_slot()) == 0u) {
       uint32_t items = 0;
       for (int item = int(cluster_id_x()); item < p.num_items; item += int(num_clusters_x())) ++items;
+#if B200FA_CAUSAL
+      uint32_t want = 0;
+      for (int item = int(cluster_id_x()); item < p.num_items; item += int(num_clusters_x()))
+        want += uint32_t(item_blocks_causal(p, item));
+      (void)items;
+#else
       const uint32_t want = items * uint32_t(p.n_kv);
+#endif
       const uint32_t groups = ld_volatile_shared(sm.count_slot(4)) + ld_volatile_shared(sm.count_slot(5));
       bool same = ld_volatile_shared(sm.count_slot(2)) == want && groups == want;
       if (rank == 0) same = same && ld_volatile_shared(sm.count_slot(0)) == want && ld_volatile_shared(sm.count_slot(1)) == want;

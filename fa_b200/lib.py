@@ -25,6 +25,7 @@ FLAG_TEST_WITHHOLD_P = 2
 FLAG_TIMELINE = 4
 FLAG_CAPTURE = 8
 FLAG_TEST_BOUNDS = 16
+FLAG_CAUSAL = 32
 BLOCK_KEYS = 128
 
 DEV_OK = 0

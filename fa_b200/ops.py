@@ -83,10 +83,14 @@ class Operator:
 
     def __call__(self, q, k, v, *, scale: float | None = None, out: torch.Tensor | None = None,
                  unit_range: tuple[int, int] | None = None, flags: int = 0,
-                 capture: torch.Tensor | None = None) -> torch.Tensor:
-        """O = softmax(Q K^T * scale) V.  ``capture`` (FP32, at least
+                 capture: torch.Tensor | None = None, causal: bool = False) -> torch.Tensor:
+        """O = softmax(Q K^T * scale) V.  ``causal``: query row i attends keys
+        0..i only (top-left aligned, as torch's ``is_causal``; an addition,
+        the reference's operator is non-causal).  ``capture`` (FP32, at least
         ``capture_bytes(...)`` bytes, on Q's device) turns on the debug
         capture of the per-block online-softmax state (``capture_view``)."""
+        if causal:
+            flags |= lib.FLAG_CAUSAL
         B, Hq, Hkv, Nq, Nk = _geometry(q, k, v)
         if out is None:
             out = torch.empty_like(q)
@@ -113,7 +117,7 @@ class Operator:
 
     def forward_host(self, q_host, k_host, v_host, out_host, *, q_dev, k_dev, v_dev, o_dev,
                      scale: float | None = None, unit_range: tuple[int, int] | None = None,
-                     chunks: int = 3) -> tuple[int, int]:
+                     chunks: int = 3, causal: bool = False) -> tuple[int, int]:
         """O = attention(Q, K, V) from pinned host buffers into a pinned host
         buffer, with the copies overlapped with the kernel.
 
@@ -180,7 +184,7 @@ class Operator:
                 ev_q.append(s_in.record_event())
         for c in range(n):
             cur.wait_event(ev_q[c])
-            self(q_dev, k_dev, v_dev, scale=scale, out=o_dev, unit_range=(bounds[c], bounds[c + 1]))
+            self(q_dev, k_dev, v_dev, scale=scale, out=o_dev, unit_range=(bounds[c], bounds[c + 1]), causal=causal)
             s_out.wait_stream(cur)
             r0, r1 = row_range(bounds[c], bounds[c + 1], Nq)
             with torch.cuda.stream(s_out):

@@ -117,6 +117,12 @@ extern "C" {
  * before the copy is issued and the kernel reports B200FA_DEV_BOUNDS.  The
  * product build ignores the flag (it has no checks and never offsets). */
 #define B200FA_FLAG_TEST_BOUNDS   16u
+/* Causal mask (top-left aligned, as torch's is_causal): query row i attends
+ * keys 0..i only.  Key blocks past the diagonal of a work item's last query
+ * block are skipped; the block that crosses a row's diagonal is masked.
+ * Runs separate kernels (b200_fa_fp{16,32}_causal_kernel); not combined
+ * with B200FA_FLAG_CAPTURE (B200FA_ERR_OPTIONS). */
+#define B200FA_FLAG_CAUSAL        32u
 #define B200FA_BLOCK_KEYS        128
 
 typedef struct b200fa_options {

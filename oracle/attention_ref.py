@@ -53,8 +53,12 @@ def _expand_kv(k: torch.Tensor, v: torch.Tensor, heads_q: int):
 
 @torch.no_grad()
 def attention_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None,
-                   rows_per_block: int = 1024) -> torch.Tensor:
-    """FP32 O[B,Hq,Nq,D] = softmax(Q K^T * scale) V, on q's device."""
+                   rows_per_block: int = 1024, causal: bool = False) -> torch.Tensor:
+    """FP32 O[B,Hq,Nq,D] = softmax(Q K^T * scale) V, on q's device.
+
+    ``causal``: query row i attends keys 0..i (top-left aligned mask, the
+    convention of torch's ``is_causal``) -- the B200 build's optional causal
+    mode; the reference operator itself is non-causal."""
     B, Hq, Nq, D = q.shape
     Hkv = k.shape[1]
     G = Hq // Hkv
@@ -72,6 +76,10 @@ def attention_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
                 for r0 in range(0, Nq, rows_per_block):
                     qf = q[b, h, r0:r0 + rows_per_block].float()
                     s = (qf @ kf.T) * scale
+                    if causal:
+                        rows = torch.arange(r0, r0 + qf.shape[0], device=s.device)[:, None]
+                        cols = torch.arange(kf.shape[0], device=s.device)[None, :]
+                        s = s.masked_fill(cols > rows, float("-inf"))
                     s -= s.amax(dim=-1, keepdim=True)
                     p = torch.exp(s)
                     out[b, h, r0:r0 + rows_per_block] = (p @ vf) / p.sum(dim=-1, keepdim=True)

@@ -157,6 +157,7 @@ def test_python_constants_match_the_header():
         "B200FA_FLAG_TIMELINE": lib.FLAG_TIMELINE,
         "B200FA_FLAG_CAPTURE": lib.FLAG_CAPTURE,
         "B200FA_FLAG_TEST_BOUNDS": lib.FLAG_TEST_BOUNDS,
+        "B200FA_FLAG_CAUSAL": lib.FLAG_CAUSAL,
         "B200FA_BLOCK_KEYS": lib.BLOCK_KEYS,
         "B200FA_DEV_OK": lib.DEV_OK,
         "B200FA_DEV_TIMEOUT": lib.DEV_TIMEOUT,
