@@ -10,7 +10,8 @@ takes the bounded abort path; no out-of-range access is issued.
 
 CPU: the checking build compiles and exports the whole C ABI.  GPU: it gives
 the product build's output bit for bit with a clean status over ragged and
-GQA shapes, and the planted out-of-range Q coordinate (B200FA_FLAG_TEST_BOUNDS,
+GQA shapes, with and without the causal mask (whose per-item block counts
+the exit check then verifies), and the planted out-of-range Q coordinate (B200FA_FLAG_TEST_BOUNDS,
 checked but never used for a copy) is caught as B200FA_DEV_BOUNDS at check
 0x81 while the product build, which has no checks, ignores the flag.
 """
@@ -37,9 +38,10 @@ SHAPES = [(1, 2, 1, 128, 128), (1, 4, 2, 300, 77), (2, 6, 3, 1000, 1029), (1, 12
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
 @pytest.mark.parametrize("variant", ["fp16", "fp32"])
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_debug_build_matches_product_with_clean_status(variant, shape):
+def test_debug_build_matches_product_with_clean_status(variant, shape, causal):
     import torch
 
     from fa_b200.ops import Operator
@@ -52,8 +54,8 @@ def test_debug_build_matches_product_with_clean_status(variant, shape):
     v = torch.randn((B, Hkv, Nk, 128), device=dev, generator=g).half()
     prod = Operator(variant)
     dbg = Operator(variant, debug=True)
-    a = prod(q, k, v)
-    b = dbg(q, k, v)
+    a = prod(q, k, v, causal=causal)
+    b = dbg(q, k, v, causal=causal)
     torch.cuda.synchronize(dev)
     assert dbg.status(dev)[0] == lib.DEV_OK, dbg.status(dev)
     assert prod.status(dev)[0] == lib.DEV_OK
