@@ -57,3 +57,20 @@ def test_bench_checks_times_and_reports(tmp_path):
         assert r["Check"] == "PASS", r
         assert float(r["MaxDiff"]) <= 2e-3 and float(r["MeanDiff"]) <= 2e-4, r
         assert float(r["Avg_us"]) > 0 and float(r["TFLOPS"]) > 0, r
+
+
+@pytest.mark.gpu
+def test_vendor_attention_is_checked_and_timed_beside_the_b200_kernels(tmp_path):
+    """cuDNN's fused attention (torch SDPA) through the same harness flow:
+    checked against the FP32 reference and timed, like the reference
+    harness's vendor operator row."""
+    res = _run(["fa_b200.core.runner", "--backend", "torch_sdpa", "--case-index", "3", "--mode", "check"])
+    assert res.returncode == 0, res.stdout + res.stderr
+    res = _run(["fa_b200.core.bench", "--backends", "b200_fa_fp16,torch_sdpa,torch_fp32_ref", "--cases", "3",
+                "--iters", "3", "--devices", "0", "--logdir", str(tmp_path)])
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    with open(next(tmp_path.glob("bench_*/report.csv")), newline="") as f:
+        rows = {r["Backend"]: r for r in csv.DictReader(f)}
+    r = rows["torch_sdpa"]
+    assert r["Check"] == "PASS", r
+    assert float(r["Avg_us"]) > 0 and float(r["TFLOPS"]) > 0, r

@@ -127,6 +127,21 @@ class RegistryTests(unittest.TestCase):
         self.assertTrue(mod.META.is_reference)
         self.assertEqual(registry.name_of(registry.get("b200_fa_fp16")), "b200_fa_fp16")
 
+    def test_vendor_attention_backend_is_discovered_and_expands_kv_heads(self):
+        from fa_b200.problem.cases import CASES
+
+        spec = registry.get("torch_sdpa")
+        self.assertFalse(spec.META.is_reference)
+        self.assertEqual(spec.META.type, "external")
+        case = CASES[3]  # Hq = 12, Hkv = 1
+        k = torch.arange(2 * 8 * 128, dtype=torch.float16).reshape(1, 2, 8, 128)[:, :1]
+        args = spec.adapt(case, {"q": torch.zeros(1, 12, 8, 128, dtype=torch.float16), "k": k, "v": k + 1})
+        self.assertEqual(tuple(args["k"].shape), (1, 12, 8, 128))
+        for h in range(12):
+            self.assertTrue(torch.equal(args["k"][0, h], k[0, 0]))
+            self.assertTrue(torch.equal(args["v"][0, h], k[0, 0] + 1))
+        self.assertEqual(args["scale"], case.scale)
+
     def test_registry_rejects_unregistered_or_ambiguous_module(self):
         spec = SimpleNamespace(META=SimpleNamespace(is_reference=False))
         for registered in ({}, {"one": spec, "two": spec}):
