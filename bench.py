@@ -28,6 +28,10 @@ Reported:
               around each launch) against the measured bf16 dense peak
   cpu_baseline the oracle's FP32 PyTorch attention on the host cores over a
               bounded sample (N=1, rank 0 only)
+  library_baseline  the GPU vendor's fused attention on the same inputs and
+              GPU after the timed region (cuDNN through torch SDPA, K/V
+              expanded to Hq heads outside its timing; N=1, rank 0 only): a
+              reference point, not part of this build's path
   clocks      nvidia-smi samples taken during the timed region
   parity      after the timed region, the timed O checked against FP32
               attention of sampled query rows (first/last rows of every
@@ -72,6 +76,7 @@ def parse_args():
     p.add_argument("--e2e-chunks", type=int, default=3,
                    help="pieces of the unit range whose copies overlap the kernel in the e2e leg")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-library-baseline", action="store_true")
     p.add_argument("--no-verify", action="store_true",
                    help="skip the post-timing parity check of the timed O (and its NCCL gather)")
     p.add_argument("--verify-rows", type=int, default=64)
@@ -237,6 +242,40 @@ def sample_rows(B, Hq, N, world, n_rows, seed=7):
         bh, i = divmod(row, N)
         picks.append((bh // Hq, bh % Hq, i))
     return picks[:max(n_rows, 2 * world)]
+
+
+def library_baseline(q, k, v, group, flops, reps=3):
+    """cuDNN's fused attention (torch SDPA restricted to the cuDNN backend) on
+    the bench's inputs, timed with CUDA events: median of ``reps`` calls
+    after two warm-ups.  Returns the JSON object, or {"unavailable": why}."""
+    import statistics
+
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    try:
+        ke = k.repeat_interleave(group, dim=1) if group > 1 else k
+        ve = v.repeat_interleave(group, dim=1) if group > 1 else v
+        times = []
+        with torch.no_grad(), sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            for _ in range(2):
+                F.scaled_dot_product_attention(q, ke, ve)
+            torch.cuda.synchronize()
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                F.scaled_dot_product_attention(q, ke, ve)
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+        del ke, ve
+        ms = statistics.median(times)
+        return {"name": "cuDNN SDPA through torch (SDPBackend.CUDNN_ATTENTION), K/V expanded to Hq heads",
+                "value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOPS", "ms_per_step": round(ms, 3),
+                "reps": reps}
+    except Exception as e:  # a reference point only: its absence does not fail the bench
+        return {"unavailable": str(e).splitlines()[0][:200] if str(e) else type(e).__name__}
 
 
 def run_reference(args, B, Hq, Hkv, N):
@@ -410,6 +449,10 @@ def main():
                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d_local,
                "d2h_bytes_per_step": d2h_local, "output_equals_device_path": bool(same.item() == 1.0)}
 
+    libref = None
+    if rank == 0 and world == 1 and not args.no_library_baseline:
+        libref = library_baseline(q, k, v, Hq // Hkv, flops_case)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle.attention_ref import cpu_time_sample
@@ -466,6 +509,7 @@ def main():
             "launch_ms_max_rank": round(launch_ms_max, 3),
         },
         "cpu_baseline": cpu,
+        "library_baseline": libref,
         "e2e": e2e,
         "parity": parity,
         "gpu_launches": args.steps,
