@@ -915,11 +915,17 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
 #else
       const bool tail = (j == n - 1 && p.nk_tail < kBlockN);
 #endif
+      // The scores: one 128-column load in the FP16 kernel, four 32-column
+      // loads in the FP32 kernel (each measured the faster for its kernel).
       uint32_t r[kBlockN];
-      tmem_ld32(tS, r);
-      tmem_ld32(tS + 32u, r + 32);
-      tmem_ld32(tS + 64u, r + 64);
-      tmem_ld32(tS + 96u, r + 96);
+      if constexpr (kVariant == 0) {
+        tmem_ld128(tS, r);
+      } else {
+        tmem_ld32(tS, r);
+        tmem_ld32(tS + 32u, r + 32);
+        tmem_ld32(tS + 64u, r + 64);
+        tmem_ld32(tS + 96u, r + 96);
+      }
       // While the scores are on their way: the reference after block j-1
       // ("ref" gb-1, published by the other group).  Waited for also at an
       // item's first block (value unused): the wait orders this group's
@@ -1008,8 +1014,12 @@ __device__ void softmax_role(const FwdParams& p, const Smem& sm, uint32_t tmem_b
       // P buffer b is free once PV of block gb - 2 completed.
       if (gb >= 2 && !wait_pv(gb - 2u)) { ok = false; break; }
       tc_fence_after();
-      tmem_st32(tP, pk);
-      tmem_st32(tP + 32u, pk + 32);
+      if constexpr (kVariant == 0) {  // one 64-column store / two 32-column stores, as the loads
+        tmem_st64(tP, pk);
+      } else {
+        tmem_st32(tP, pk);
+        tmem_st32(tP + 32u, pk + 32);
+      }
       tmem_wait_st();
       tl.mark(int(warp), j, 5);
       tc_fence_before();
