@@ -73,8 +73,10 @@ def parse_args():
     p.add_argument("--shape", type=str, default="2,12,1,131072",
                    help="B,Hq,Hkv,N (default: the headline metric config)")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--e2e-chunks", type=int, default=3,
-                   help="pieces of the unit range whose copies overlap the kernel in the e2e leg")
+    p.add_argument("--e2e-chunks", type=int, default=0,
+                   help="pieces of the unit range whose copies overlap the kernel in the e2e leg "
+                        "(0: 6 for a range of at least 16384 units, else 3 -- the faster of the two, "
+                        "measured at the ranges of 1/2/4/8-GPU runs of the headline config)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-library-baseline", action="store_true")
     p.add_argument("--no-verify", action="store_true",
@@ -413,6 +415,7 @@ def main():
         v_host.copy_(v)
         o_host = torch.empty((r1 - r0, D), dtype=torch.float16, pin_memory=True)
         e2e_steps = max(1, min(args.steps, 5))
+        e2e_chunks = args.e2e_chunks or (6 if ue - ub >= 16384 else 3)
 
         moved = [0, 0]
 
@@ -421,7 +424,7 @@ def main():
             # heads and Q rows up, the kernel, its O rows down; the copies
             # overlap the other pieces' kernels.
             moved[:] = op.forward_host(q_host, k_host, v_host, o_host, q_dev=q, k_dev=k, v_dev=v, o_dev=o,
-                                       unit_range=(ub, ue), chunks=args.e2e_chunks)
+                                       unit_range=(ub, ue), chunks=e2e_chunks)
 
         e2e_step()
         barrier(world)
@@ -447,7 +450,8 @@ def main():
             dist.all_reduce(same, op=dist.ReduceOp.MIN)
         e2e = {"value": round(flops_case / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d_local,
-               "d2h_bytes_per_step": d2h_local, "output_equals_device_path": bool(same.item() == 1.0)}
+               "d2h_bytes_per_step": d2h_local, "pieces": e2e_chunks,
+               "output_equals_device_path": bool(same.item() == 1.0)}
 
     libref = None
     if rank == 0 and world == 1 and not args.no_library_baseline:
