@@ -49,7 +49,10 @@ def test_oracle_causal_mask_is_torchs_is_causal():
     ref = attention_fp32(q, k, v, causal=True, rows_per_block=32)
     kk, vv = k.repeat_interleave(2, dim=1), v.repeat_interleave(2, dim=1)
     sdpa = torch.nn.functional.scaled_dot_product_attention(q.float(), kk.float(), vv.float(), is_causal=True)
-    assert torch.allclose(ref, sdpa, atol=2e-6, rtol=0)
+    # Two FP32 implementations (their summation order follows torch's CPU
+    # threading): agreement to 1e-5, where a mask off by one key or row
+    # differs by ~1e-2.
+    assert torch.allclose(ref, sdpa, atol=1e-5, rtol=0), float((ref - sdpa).abs().max())
 
 
 @pytest.mark.gpu
